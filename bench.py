@@ -1,0 +1,344 @@
+"""Benchmark of the routed-expert hot path on B200.
+
+One step = one MoE layer of the Qwen3-30B-A3B shape (config 2 of the
+benchmark: d_model 2048, 128 experts, top-8, expert intermediate 768, int4
+group-32 experts with f16 scales) over a decode batch of T tokens: router
+logits -> softmax top-k -> permute by expert -> fused gate|up/SiLU/down
+mat-vecs over the packed experts -> weighted combine.  Synthetic seeded
+inputs (numpy PCG64) with the benchmark's shapes and distributions.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl reference]
+
+Prints one JSON line (rank 0).  ``--impl reference`` times the reference's
+CPU algorithm for the same step (the oracle restatement in oracle/, with all
+host threads) instead of the GPU.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+if "--impl" in sys.argv and "reference" in sys.argv:
+    # the reference runs BLAS single-threaded and parallelises over experts
+    os.environ.setdefault("OPENBLAS_NUM_THREADS", "1")
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+H, I, E, K_TOP, GS = 2048, 768, 128, 8, 32
+EXPERT_BYTES = 2 * I * H // 2 + 2 * I * (H // GS) * 2 + H * I // 2 + H * (I // GS) * 2   # 2,654,208
+METRIC = "moe_layer_tokens_per_s"
+UNIT = "tokens/s"
+L2_ROTATE_LAYERS = 4
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--tokens", type=int, default=64)
+    p.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    p.add_argument("--no-sweep", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def make_experts(seed=0):
+    from distributedmoellm_b200 import synthetic as S
+    rng = np.random.default_rng(seed)
+    experts = {e: S.int4_expert(rng, H, I, GS, f16_scales=True) for e in range(E)}
+    router = S.router(rng, E, H)
+    return experts, router
+
+
+# ---- clocks sampled during the timed region ------------------------------------------
+
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx, self.rows, self.proc = gpu_index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([v.strip() for v in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 5 + i and r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ---- CPU side: the reference's algorithm (oracle restatement) -----------------------------
+
+def cpu_step_fn(experts, router, T, seed=7):
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+    desc = {e: (("q4", gr, gsc.astype(np.float32), GS, False), ("q4", dr, dsc.astype(np.float32), GS, False))
+            for e, (gr, gsc, dr, dsc) in experts.items()}
+    x = np.random.default_rng(seed).standard_normal((T, H), dtype=np.float32)
+
+    def step():
+        return O.moe_layer(x, router, desc, K_TOP, True, I)[0]
+    return step, O
+
+
+def time_cpu(step, budget_s=12.0, max_steps=200):
+    step()  # warm (thread pools, page-in)
+    n, t0 = 0, time.perf_counter()
+    while n < max_steps and (n == 0 or time.perf_counter() - t0 < budget_s):
+        step()
+        n += 1
+    return (time.perf_counter() - t0) / n, n
+
+
+# ---- GPU side ---------------------------------------------------------------------------------
+
+def build_layers(experts, router, dev, n_layers):
+    import torch
+    from distributedmoellm_b200 import layout as L
+    from distributedmoellm_b200.layer import MoELayer
+    from distributedmoellm_b200.store import LayerExperts
+    base = LayerExperts(E, H, I, GS, L.FMT_Q4_F16, L.FMT_Q4_F16, dev)
+    for e, (gr, gsc, dr, dsc) in experts.items():
+        base.put_int4(e, gr, gsc, dr, dsc, offset=False)
+    base.publish()
+    rt = torch.from_numpy(router).to(dev)
+    layers = [MoELayer(rt, base, K_TOP, True)]
+    for _ in range(n_layers - 1):          # same bytes at other addresses: each step streams from HBM
+        ex = LayerExperts(E, H, I, GS, L.FMT_Q4_F16, L.FMT_Q4_F16, dev)
+        ex.buf.copy_(base.buf)
+        off = ex.buf.data_ptr() - base.buf.data_ptr()
+        ex._table_host = base._table_host + np.where(base._table_host != 0, off, 0)
+        ex.present = set(base.present)
+        ex.publish()
+        layers.append(MoELayer(rt, ex, K_TOP, True))
+    return layers
+
+
+def run_gpu(args, rank, world, dev):
+    import torch
+    import torch.distributed as dist
+    from distributedmoellm_b200 import device as D
+    D.require_device()
+    experts, router = make_experts(0)
+    layers = build_layers(experts, router, dev, L2_ROTATE_LAYERS)
+    pk, pk_kind = peaks()
+
+    def measure(T, steps, warmup, decode_events=True):
+        rng = np.random.default_rng(1000 + 17 * rank + T)
+        xs = [torch.from_numpy(rng.standard_normal((T, H), dtype=np.float32)).to(dev) for _ in range(len(layers))]
+        # unique experts of each (layer, batch) pair, for the algorithmic bytes
+        uniq = []
+        for l, x in zip(layers, xs):
+            b = l.route(x)
+            torch.cuda.synchronize()
+            uniq.append(int(b.routing.n_unique.item()))
+        for i in range(warmup):
+            layers[i % len(layers)](xs[i % len(layers)])
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for i in range(steps):
+            l = layers[i % len(layers)]
+            x = xs[i % len(layers)]
+            b = l.route(x)
+            if decode_events:
+                ev[i][0].record()
+            l.experts_forward(x, b)
+            if decode_events:
+                ev[i][1].record()
+            D.combine(b.y, b.routing.inv, b.w.view(-1), T, K_TOP, out=b.out)
+        stop.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = start.elapsed_time(stop) / steps
+        dec_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev) if decode_events else None
+        u_avg = statistics.mean(uniq[i % len(layers)] for i in range(steps))
+        status = max(int(l.status(T)) for l in layers)
+        return ms, dec_ms, u_avg, status
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    T = args.tokens
+    with Clocks(int(str(dev).split(":")[-1]) if ":" in str(dev) else 0) as clk:
+        ms, dec_ms, u_avg, status = measure(T, args.steps, args.warmup)
+    ms = max_over_ranks(ms)
+    value = world * T / (ms / 1e3)
+
+    # roofline of the dominant kernel (the fused decode: both phases)
+    alg_bytes = u_avg * EXPERT_BYTES + T * H * 4 + T * K_TOP * H * 4
+    achieved = alg_bytes / (dec_ms / 1e3) / 1e9
+    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None, "peak_kind": pk_kind,
+            "kernel": "moe_decode_kernel (gate|up + down phases)", "kernel_ms": round(dec_ms, 5),
+            "alg_bytes_per_launch": int(alg_bytes), "unique_experts": u_avg}
+
+    # end to end through the public API with host buffers (pinned), H2D + D2H inside the timed region
+    e2e = measure_e2e(layers, T, args.steps, args.warmup, world, dev)
+    e2e["value"] = world * T / (max_over_ranks(e2e.pop("ms")) / 1e3)
+
+    sweep = {}
+    if not args.no_sweep:
+        for Ts in (1, 8, 32, 64):
+            if Ts == T:
+                continue
+            m, dm, u, st = measure(Ts, max(10, args.steps // 2), 3)
+            ab = u * EXPERT_BYTES + Ts * H * 4 + Ts * K_TOP * H * 4
+            sweep[f"decode_T{Ts}"] = {"tokens_per_s": round(world * Ts / (max_over_ranks(m) / 1e3), 1),
+                                      "ms_per_step": round(m, 5), "kernel_ms": round(dm, 5),
+                                      "hbm_frac": round(ab / (dm / 1e3) / 1e9 / pk["hbm_gbs"], 4),
+                                      "unique_experts": u}
+            status = max(status, st)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        step, O = cpu_step_fn(experts, router, T)
+        s_per, n = time_cpu(step)
+        cpu = {"value": round(T / s_per, 2), "unit": UNIT, "cores": O.threads(), "kind": "port",
+               "sample": f"{n} MoE-layer steps of T={T} tokens (all 128 experts resident in host RAM), "
+                         f"C+OpenMP restatement of moelan's fused int4 layer kernel + numpy routing"}
+    return value, ms, roof, e2e, sweep, cpu, clk.summary(), status
+
+
+def measure_e2e(layers, T, steps, warmup, world, dev):
+    import torch
+    import torch.distributed as dist
+    rng = np.random.default_rng(999)
+    hx = [torch.from_numpy(rng.standard_normal((T, H), dtype=np.float32)).pin_memory() for _ in layers]
+    hout = torch.empty((T, H), dtype=torch.float32).pin_memory()
+    dx = [torch.empty((T, H), dtype=torch.float32, device=dev) for _ in layers]
+
+    def step(i):
+        l = layers[i % len(layers)]
+        x = dx[i % len(layers)]
+        x.copy_(hx[i % len(layers)], non_blocking=True)
+        out = l(x)
+        hout.copy_(out, non_blocking=True)
+
+    for i in range(warmup):
+        step(i)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(steps):
+        step(i)
+    b.record()
+    torch.cuda.synchronize()
+    return {"ms": a.elapsed_time(b) / steps, "unit": UNIT, "h2d_bytes_per_step": T * H * 4,
+            "d2h_bytes_per_step": T * H * 4, "api": "distributedmoellm_b200.layer.MoELayer.forward"}
+
+
+def run_reference(args):
+    """The reference arm: moelan's CPU algorithm (oracle restatement) on the host cores."""
+    experts, router = make_experts(0)
+    step, O = cpu_step_fn(experts, router, args.tokens)
+    for _ in range(max(1, args.warmup)):
+        step()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * statistics.mean(times)
+    value = args.tokens / (ms / 1e3)
+    return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "impl": "reference",
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args),
+            "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": O.threads(), "kind": "port",
+                             "sample": f"{args.steps} MoE-layer steps of T={args.tokens}"},
+            "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def workload_config(args):
+    return {"workload": f"qwen3-30b-a3b moe layer decode, T={args.tokens} tokens/step per GPU",
+            "d_model": H, "experts": E, "top_k": K_TOP, "expert_inter": I, "weights": "int4 g32 f16 scales",
+            "tokens_per_gpu": args.tokens, "parallelism": f"replicas{args.gpus}" if args.gpus > 1 else "single",
+            "l2": f"{L2_ROTATE_LAYERS} layers of experts rotated per step (each ~340 MB > 126 MB L2)"}
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return
+    import torch
+    import torch.distributed as dist
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    value, ms, roof, e2e, sweep, cpu, clocks, status = run_gpu(args, rank, world, dev)
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32 activations x int4 weights (f16 tensor-core pieces, f32 accum)",
+                "data": "synthetic", "config": workload_config(args), "roofline": roof, "cpu_baseline": cpu,
+                "e2e": e2e, "clocks": clocks, "gpu_launches": 6 * args.steps, "sweep": sweep,
+                "kernel_status": status}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

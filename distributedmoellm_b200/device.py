@@ -1,0 +1,168 @@
+"""Device-level entry points: thin wrappers that pass torch CUDA tensors to
+the C ABI (libmoelan_b200.so) on the current stream.  Every function raises
+RuntimeError when the library reports an error; nothing here computes on the
+CPU."""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import check, lib
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and (not t.is_cuda or not t.is_contiguous()):
+            raise RuntimeError("expected contiguous CUDA tensors")
+
+
+_checked_devices: set = set()
+
+
+def require_device() -> None:
+    """Raise unless a CUDA device this library is built for (sm_100) is current."""
+    if not torch.cuda.is_available():
+        raise RuntimeError("distributedmoellm_b200 needs a CUDA device (sm_100a); none is available")
+    dev = torch.cuda.current_device()
+    if dev not in _checked_devices:
+        check(lib().mb_device_check(), "mb_device_check")
+        _checked_devices.add(dev)
+
+
+# ---- dequantisation ----------------------------------------------------------------
+
+def q4_dequant(raw: torch.Tensor, s: torch.Tensor, gs: int, offset: bool, out: torch.Tensor | None = None):
+    _cuda(raw, s)
+    O, C = raw.shape
+    out = torch.empty((O, 2 * C), dtype=torch.float32, device=raw.device) if out is None else out
+    check(lib().mb_q4_dequant(_p(raw), _p(s), int(s.dtype == torch.float16), O, 2 * C, gs,
+                              0 if offset else 0x88, _p(out), _stream()), "mb_q4_dequant")
+    return out
+
+
+def q8_dequant(q: torch.Tensor, s: torch.Tensor, gs: int, out: torch.Tensor | None = None):
+    _cuda(q, s)
+    O, K = q.shape
+    out = torch.empty((O, K), dtype=torch.float32, device=q.device) if out is None else out
+    check(lib().mb_q8_dequant(_p(q), _p(s), int(s.dtype == torch.float16), O, K, gs, _p(out), _stream()),
+          "mb_q8_dequant")
+    return out
+
+
+def gguf_dequant(raw: torch.Tensor, qtype: int, cols: int, out: torch.Tensor | None = None):
+    _cuda(raw)
+    out = torch.empty((raw.shape[0], cols), dtype=torch.float32, device=raw.device) if out is None else out
+    check(lib().mb_gguf_dequant(_p(raw), int(qtype), raw.shape[0], raw.shape[1], cols, _p(out), _stream()),
+          "mb_gguf_dequant")
+    return out
+
+
+# ---- router -------------------------------------------------------------------------
+
+def router_logits(x: torch.Tensor, router: torch.Tensor, logits=None, row_exp=None):
+    _cuda(x, router)
+    T, H = x.shape
+    E = router.shape[0]
+    logits = torch.empty((T, E), dtype=torch.float32, device=x.device) if logits is None else logits
+    check(lib().mb_router_logits(_p(x), _p(router), T, H, E, _p(logits), _p(row_exp), _stream()),
+          "mb_router_logits")
+    return logits
+
+
+def row_exponents(x: torch.Tensor, out=None):
+    _cuda(x)
+    out = torch.empty(x.shape[0], dtype=torch.int32, device=x.device) if out is None else out
+    check(lib().mb_row_exponents(_p(x), x.shape[0], x.shape[1], _p(out), _stream()), "mb_row_exponents")
+    return out
+
+
+def router_topk(logits: torch.Tensor, k: int, normalize: bool, idx=None, w=None):
+    _cuda(logits)
+    T, E = logits.shape
+    idx = torch.empty((T, k), dtype=torch.int32, device=logits.device) if idx is None else idx
+    w = torch.empty((T, k), dtype=torch.float32, device=logits.device) if w is None else w
+    check(lib().mb_router_topk(_p(logits), T, E, k, int(bool(normalize)), _p(idx), _p(w), _stream()),
+          "mb_router_topk")
+    return idx, w
+
+
+class Routing:
+    """Device buffers of one permutation of T*k picks over E experts."""
+
+    def __init__(self, T: int, k: int, E: int, device):
+        P = T * k
+        i32 = dict(dtype=torch.int32, device=device)
+        self.T, self.k, self.E, self.P = T, k, E, P
+        self.counts = torch.empty(E, **i32)
+        self.offsets = torch.empty(E + 1, **i32)
+        self.sorted_rows = torch.empty(max(P, 1), **i32)
+        self.sorted_w = torch.empty(max(P, 1), dtype=torch.float32, device=device)
+        self.inv = torch.empty(max(P, 1), **i32)
+        self.uexperts = torch.empty(E, **i32)
+        self.uoffsets = torch.empty(E + 1, **i32)
+        self.n_unique = torch.empty(1, **i32)
+
+
+def permute(idx: torch.Tensor, w: torch.Tensor | None, E: int, r: Routing | None = None) -> Routing:
+    _cuda(idx, w)
+    T, k = idx.shape
+    r = Routing(T, k, E, idx.device) if r is None else r
+    check(lib().mb_permute(_p(idx), _p(w), T, k, E, _p(r.counts), _p(r.offsets), _p(r.sorted_rows),
+                           _p(r.sorted_w), _p(r.inv), _p(r.uexperts), _p(r.uoffsets), _p(r.n_unique),
+                           _stream()), "mb_permute")
+    return r
+
+
+def combine(y: torch.Tensor, pair_idx: torch.Tensor, pair_w: torch.Tensor, T: int, k: int,
+            out: torch.Tensor | None = None, accumulate: bool = False, row_ptr: torch.Tensor | None = None):
+    """out[r] (+)= sum of pair_w[i] * y[pair_idx[i]] over row r's entries."""
+    _cuda(y, pair_idx, pair_w, row_ptr)
+    H = y.shape[1]
+    out = torch.empty((T, H), dtype=torch.float32, device=y.device) if out is None else out
+    check(lib().mb_unpermute_combine(_p(y), _p(row_ptr), _p(pair_idx), _p(pair_w), T, k, H, int(accumulate),
+                                     _p(out), _stream()), "mb_unpermute_combine")
+    return out
+
+
+# ---- fused decode -------------------------------------------------------------------
+
+def decode_workspace_bytes(P: int, I: int) -> int:
+    return int(lib().mb_moe_decode_workspace_bytes(P, I))
+
+
+def moe_decode(table: torch.Tensor, E: int, H: int, I: int, gs: int, fmt_gu: int, fmt_down: int, x: torch.Tensor,
+               row_exp: torch.Tensor, r: Routing, y: torch.Tensor, workspace: torch.Tensor, max_rows: int = 0,
+               status: torch.Tensor | None = None):
+    _cuda(table, x, row_exp, y, workspace, status)
+    check(lib().mb_moe_decode(_p(table), E, H, I, gs, fmt_gu, fmt_down, _p(x), _p(row_exp), x.shape[0],
+                              _p(r.counts), _p(r.offsets), _p(r.sorted_rows), r.P, int(max_rows), _p(y),
+                              _p(workspace), workspace.numel() * workspace.element_size(), _p(status), _stream()),
+          "mb_moe_decode")
+    return y
+
+
+def matmul_t(w_tiles: torch.Tensor, fmt: int, O: int, K: int, x: torch.Tensor, y: torch.Tensor | None = None,
+             workspace: torch.Tensor | None = None, status: torch.Tensor | None = None):
+    """x @ W.T for one matrix in the tile layout."""
+    _cuda(w_tiles, x, y, workspace, status)
+    n = x.shape[0]
+    y = torch.empty((n, O), dtype=torch.float32, device=x.device) if y is None else y
+    if workspace is None:
+        workspace = torch.empty(int(lib().mb_matmul_t_workspace_bytes(n)), dtype=torch.uint8, device=x.device)
+    check(lib().mb_matmul_t(_p(w_tiles), fmt, O, K, _p(x), n, _p(y), _p(workspace), workspace.numel(), _p(status),
+                            _stream()), "mb_matmul_t")
+    return y
+
+
+__all__ = [n for n in dir() if not n.startswith("_")] + ["_lib"]

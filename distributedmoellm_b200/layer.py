@@ -1,0 +1,74 @@
+"""One MoE layer on the device: router logits -> top-k -> permute by expert ->
+fused expert mat-vecs -> weighted combine, every step a kernel of
+libmoelan_b200.so on the current stream.
+
+This is the device-side form of moelan/model.py:593-606 (_ffn: logits,
+route, backend.moe) with a local backend (model.py:267-278) and
+ExpertStore.compute (moelan/experts.py:641-670).  All buffers for a given
+token count are allocated once and reused, so a forward can be captured in
+a CUDA graph.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import device as D
+from .store import LayerExperts
+
+
+class _Buffers:
+    def __init__(self, T: int, E: int, k: int, H: int, I: int, dev):
+        P = T * k
+        self.logits = torch.empty((T, E), dtype=torch.float32, device=dev)
+        self.row_exp = torch.empty(T, dtype=torch.int32, device=dev)
+        self.idx = torch.empty((T, k), dtype=torch.int32, device=dev)
+        self.w = torch.empty((T, k), dtype=torch.float32, device=dev)
+        self.routing = D.Routing(T, k, E, dev)
+        self.y = torch.empty((max(P, 1), H), dtype=torch.float32, device=dev)
+        self.ws = torch.empty(D.decode_workspace_bytes(P, I), dtype=torch.uint8, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.out = torch.empty((T, H), dtype=torch.float32, device=dev)
+
+
+class MoELayer:
+    """``router`` (E, H) f32 on the device; ``experts`` the layer's packed experts."""
+
+    def __init__(self, router: torch.Tensor, experts: LayerExperts, top_k: int, normalize: bool = True):
+        self.router = router.contiguous()
+        self.experts = experts
+        self.E, self.H, self.I = experts.E, experts.H, experts.I
+        self.k, self.normalize = top_k, normalize
+        self._bufs: dict[int, _Buffers] = {}
+
+    def buffers(self, T: int) -> _Buffers:
+        b = self._bufs.get(T)
+        if b is None:
+            b = self._bufs[T] = _Buffers(T, self.E, self.k, self.H, self.I, self.router.device)
+        return b
+
+    def route(self, x: torch.Tensor) -> _Buffers:
+        b = self.buffers(x.shape[0])
+        D.router_logits(x, self.router, b.logits, b.row_exp)
+        D.router_topk(b.logits, self.k, self.normalize, b.idx, b.w)
+        D.permute(b.idx, b.w, self.E, b.routing)
+        return b
+
+    def experts_forward(self, x: torch.Tensor, b: _Buffers) -> None:
+        ex = self.experts
+        D.moe_decode(ex.table, self.E, self.H, self.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, b.row_exp, b.routing,
+                     b.y, b.ws, max_rows=0, status=b.status)
+
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """out (T, H) = sum over each token's k picks of weight * expert(x)."""
+        x = x.contiguous()
+        b = self.route(x)
+        self.experts_forward(x, b)
+        T = x.shape[0]
+        return D.combine(b.y, b.routing.inv, b.w.view(-1), T, self.k, out=b.out if out is None else out)
+
+    __call__ = forward
+
+    def status(self, T: int) -> int:
+        """The kernels' status word for token count T (0 = no failure)."""
+        return int(self.buffers(T).status.item())

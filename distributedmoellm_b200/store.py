@@ -1,0 +1,78 @@
+"""Experts resident on one GPU, packed, in the device tile layout.
+
+The reference keeps experts in host RAM in their packed formats
+(moelan/experts.py:538-795, ExpertStore) and its GPU tier keeps a dequantised
+fp16 copy (moelan/accel.py:75-109).  Here a layer's experts stay packed on
+the device (2.65 MB per int4-g32-f16 Qwen3-30B expert instead of 9.4 MB of
+fp16), one slot each in a single buffer, with a table of their addresses
+(MbExpert entries) that the kernels index by expert id.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import layout
+
+ALIGN = 256
+
+
+def _al(n: int) -> int:
+    return (n + ALIGN - 1) // ALIGN * ALIGN
+
+
+class LayerExperts:
+    """One MoE layer's experts on a device.  ``ids``: the expert ids this
+    device holds (all E by default; a slice under expert parallelism)."""
+
+    def __init__(self, E: int, H: int, I: int, gs: int, fmt_gu: int, fmt_down: int, device, ids=None):
+        self.E, self.H, self.I, self.gs = E, H, I, gs
+        self.fmt_gu, self.fmt_down = fmt_gu, fmt_down
+        self.device = torch.device(device)
+        self.ids = list(range(E)) if ids is None else [int(i) for i in ids]
+        self.gu_nbytes = layout.tiles_nbytes(fmt_gu, 2 * I, H, gu_inter=I)
+        self.dn_nbytes = layout.tiles_nbytes(fmt_down, H, I)
+        self.slot_bytes = _al(self.gu_nbytes) + _al(self.dn_nbytes)
+        self.slot_of = {e: i for i, e in enumerate(self.ids)}
+        self.buf = torch.zeros(max(1, len(self.ids)) * self.slot_bytes, dtype=torch.uint8, device=self.device)
+        self._table_host = np.zeros((E, 2), np.int64)
+        self.table = torch.zeros((E, 2), dtype=torch.int64, device=self.device)
+        self.present: set[int] = set()
+
+    # ---- placement
+    def _slot(self, e: int):
+        i = self.slot_of[e]
+        base = i * self.slot_bytes
+        return base, base + _al(self.gu_nbytes)
+
+    def put_tiles(self, e: int, gu_tiles, dn_tiles) -> None:
+        """Store expert ``e`` from tile bytes (numpy on the host, or uint8 tensors)."""
+        if e not in self.slot_of:
+            raise KeyError(f"expert {e} is not placed on this device")
+        g0, d0 = self._slot(e)
+        for off, t, n in ((g0, gu_tiles, self.gu_nbytes), (d0, dn_tiles, self.dn_nbytes)):
+            src = torch.as_tensor(t) if isinstance(t, np.ndarray) else t
+            if src.numel() != n:
+                raise ValueError(f"tile bytes {src.numel()} != expected {n}")
+            self.buf[off:off + n].copy_(src.reshape(-1), non_blocking=False)
+        base = self.buf.data_ptr()
+        self._table_host[e] = (base + g0, base + d0)
+        self.present.add(e)
+
+    def put_int4(self, e: int, gu_raw, gu_s, dn_raw, dn_s, offset: bool = False) -> None:
+        """Expert ``e`` from colibri int4 arrays (moelan Packed4: raw, s)."""
+        self.put_tiles(e, layout.q4_tiles(gu_raw, gu_s, self.gs, offset, gu_inter=self.I),
+                       layout.q4_tiles(dn_raw, dn_s, self.gs, offset))
+
+    def put_int8(self, e: int, gu_q, gu_s, dn_q, dn_s) -> None:
+        """Expert ``e`` from group-scaled int8 arrays (moelan GroupQuant: q, s)."""
+        self.put_tiles(e, layout.q8_tiles(gu_q, gu_s, self.gs, gu_inter=self.I), layout.q8_tiles(dn_q, dn_s, self.gs))
+
+    def publish(self) -> None:
+        """Upload the address table after a batch of puts."""
+        self.table.copy_(torch.from_numpy(self._table_host))
+
+    @property
+    def nbytes(self) -> int:
+        return self.buf.numel()

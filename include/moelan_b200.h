@@ -1,0 +1,146 @@
+/*
+ * moelan_b200.h -- C ABI of libmoelan_b200.so, the sm_100a routed-expert path.
+ *
+ * Every entry point takes plain device pointers and sizes, a CUDA stream
+ * (cudaStream_t passed as void*, never the legacy default stream's special
+ * handles other than 0), and returns 0 (MB_OK) or an error code; the message
+ * of the last error on the calling thread is mb_last_error().  Calls are
+ * stream-ordered and asynchronous; no entry point synchronises the device.
+ * The library allocates nothing: scratch comes from caller-provided workspace
+ * whose size the *_workspace_bytes functions return.  Buffers are owned by
+ * the caller and must stay alive until the stream has run the call.
+ *
+ * Each entry point names the reference (moelan) interface it replaces.
+ * Reference paths are relative to the moelan project root.
+ */
+#ifndef MOELAN_B200_H
+#define MOELAN_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    MB_OK = 0,
+    MB_EINVAL = 1,       /* bad argument (shape, alignment, null pointer) */
+    MB_ECUDA = 2,        /* a CUDA runtime error */
+    MB_EUNSUPPORTED = 3, /* a format or size this build does not handle */
+    MB_EDEVICE = 4       /* a kernel reported a failure in its status word */
+};
+
+/* Weight formats of the device tile layout (see mb_*_relayout in the Python
+ * package and the layout notes in DESIGN.md of the repository). */
+enum {
+    MB_FMT_Q4_F32 = 1, /* int4, two nibbles per byte, group scales f32 */
+    MB_FMT_Q4_F16 = 2, /* int4, group scales f16 */
+    MB_FMT_Q8_F32 = 3, /* int8, group scales f32 */
+    MB_FMT_Q8_F16 = 4  /* int8, group scales f16 (also GGUF Q8_0 blocks) */
+};
+
+const char *mb_last_error(void);
+int mb_version(void);
+/* MB_OK when the current device is an sm_100 part this build runs on. */
+int mb_device_check(void);
+
+/* ---- dequantisation (bit-exact) -------------------------------------------- */
+
+/* moelan/kernels.py:971 q4_dequant(raw, s, gs, offset, out) -> _q4_dequant
+ * (kernels.py:215-228).  raw (rows, cols/2) u8, scales (rows, cols/gs) f32 or
+ * f16 (scale_f16 != 0), xor_mask 0x88 for two's-complement nibbles, 0 for the
+ * XOR-ed resident form.  out (rows, cols) f32. */
+int mb_q4_dequant(const uint8_t *raw, const void *scales, int scale_f16, int64_t rows, int64_t cols, int gs,
+                  uint8_t xor_mask, float *out, void *stream);
+
+/* moelan/kernels.py:976 q8_dequant(q, s, gs, out) -> _q8_dequant (kernels.py:230-237). */
+int mb_q8_dequant(const int8_t *q, const void *scales, int scale_f16, int64_t rows, int64_t cols, int gs,
+                  float *out, void *stream);
+
+/* moelan/kernels.py:1001 gguf_dequant(raw, qtype, out) and moelan/gguf.py:258
+ * dequantize -> _gguf_dequant (kernels.py:693-697).  qtype: ggml type id
+ * (2 Q4_0, 3 Q4_1, 6 Q5_0, 7 Q5_1, 8 Q8_0, 10 Q2_K, 11 Q3_K, 12 Q4_K, 13 Q5_K,
+ * 14 Q6_K). */
+int mb_gguf_dequant(const uint8_t *raw, int qtype, int64_t rows, int64_t row_bytes, int64_t cols, float *out,
+                    void *stream);
+
+/* ---- router ------------------------------------------------------------------ */
+
+/* Router logits h @ router.T (moelan/model.py:597) in f32, plus, when
+ * row_exp != NULL, each row's power-of-two exponent used by the mat-vecs. */
+int mb_router_logits(const float *x, const float *router, int64_t T, int H, int E, float *logits,
+                     int32_t *row_exp, void *stream);
+
+/* moelan/model.py:160 route(logits, top_k, normalize) with _top_k
+ * (model.py:154-157): f32 softmax, k best experts (ties: lower id first),
+ * weights renormalised when normalize != 0.  idx (T, k) i32, w (T, k) f32. */
+int mb_router_topk(const float *logits, int64_t T, int E, int k, int normalize, int32_t *idx, float *w,
+                   void *stream);
+
+/* Each row's power-of-two exponent (for inputs that did not come through
+ * mb_router_logits). */
+int mb_row_exponents(const float *x, int64_t T, int H, int32_t *row_exp, void *stream);
+
+/* moelan/model.py:226 group_by_expert(idx, w): stable counting sort of the
+ * T*k picks by expert.  Outputs (all device):
+ *   counts (E), offsets (E+1)        per expert, over all E experts
+ *   sorted_rows (T*k), sorted_w      token and weight of each sorted pick
+ *   inv (T*k)                        sorted position of pick t*k+j
+ *   uexperts (E), uoffsets (E+1), n_unique (1): the compact form the
+ *                                    reference returns (experts, offsets)
+ * T*k <= 65536, E <= 1024.  Any output pointer except counts/offsets/
+ * sorted_rows may be NULL. */
+int mb_permute(const int32_t *idx, const float *w, int64_t T, int k, int E, int32_t *counts, int32_t *offsets,
+               int32_t *sorted_rows, float *sorted_w, int32_t *inv, int32_t *uexperts, int32_t *uoffsets,
+               int32_t *n_unique, void *stream);
+
+/* The weighted combine out[r] (+)= sum_i pair_w[i] * y[pair_idx[i]] over
+ * i in [row_ptr[r], row_ptr[r+1]) in that order (the scatter-adds of
+ * moelan/experts.py:711,723,727 and kernels.py:778-782, 968).  When row_ptr
+ * is NULL each row has k consecutive entries (i = r*k .. r*k+k-1).
+ * accumulate != 0 adds into out, else overwrites.  y (P, H), out (T, H). */
+int mb_unpermute_combine(const float *y, const int32_t *row_ptr, const int32_t *pair_idx, const float *pair_w,
+                         int64_t T, int k, int H, int accumulate, float *out, void *stream);
+
+/* ---- fused decode mat-vecs over packed experts -------------------------------- */
+
+/* One expert's weights in the device tile layout: gate|up (2I, H) and down
+ * (H, I), each a pointer to its tiles (16-byte aligned). */
+typedef struct {
+    const void *gu;
+    const void *down;
+} MbExpert;
+
+/* Workspace bytes for mb_moe_decode with P = T*k picks. */
+int64_t mb_moe_decode_workspace_bytes(int64_t P, int I);
+
+/* One MoE layer's routed experts, for experts picked by at most max_rows
+ * tokens (decode): moelan/kernels.py:942 moe_q4(x, items, H, I, gs, out)
+ * (kernels.py:712-782), generalised to int8 experts (kernels.py:133-168) and
+ * GGUF Q8_0 down projections.  For each expert e with 0 < counts[e] <=
+ * max_rows, its picks offsets[e]..offsets[e+1] of the sorted order (rows of
+ * x given by sorted_rows) are run through gate|up, SiLU(gate) * up and down:
+ * y (P, H) f32 gets the unweighted expert output of each pick.  Pass row_exp
+ * from mb_router_logits / mb_row_exponents.  fmt_gu / fmt_down: MB_FMT_*.
+ * status: a device word the kernels OR MB_STATUS bits into, or NULL to use
+ * a word inside the workspace. */
+int mb_moe_decode(const MbExpert *table, int E, int H, int I, int gs, int fmt_gu, int fmt_down, const float *x,
+                  const int32_t *row_exp, int64_t T, const int32_t *counts, const int32_t *offsets,
+                  const int32_t *sorted_rows, int64_t P, int max_rows, float *y, void *workspace,
+                  int64_t workspace_bytes, unsigned *status, void *stream);
+
+/* Workspace bytes for mb_matmul_t with n input rows. */
+int64_t mb_matmul_t_workspace_bytes(int64_t n);
+
+/* x @ W.T for one packed matrix W (O, K) in the device tile layout (fmt
+ * MB_FMT_*): moelan/kernels.py:1018 q4_matmul_t and kernels.py:1030
+ * q8_matmul_t (GGUF Q8_0 rows too, as int8 tiles with f16 scales:
+ * kernels.py:981 gguf_matmul_t).  x (n, K) f32, y (n, O) f32. */
+int mb_matmul_t(const void *w_tiles, int fmt, int O, int K, const float *x, int64_t n, float *y, void *workspace,
+                int64_t workspace_bytes, unsigned *status, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOELAN_B200_H */

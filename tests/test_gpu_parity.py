@@ -1,0 +1,283 @@
+"""GPU parity of every kernel on the routed-expert path against the
+reference's own outputs (golden.npz) and the CPU oracle.
+
+Bars: dequantisation and router indices / grouping bit-exact; f32-path
+outputs within 1e-5 of the reference measured per output row as
+max|got - want| / max|want| (the reference itself runs with fastmath and
+cancels u*x*s against 8*s*sum(x), so element-wise relative error is not a
+meaningful bar near zero)."""
+
+import numpy as np
+import pytest
+import torch
+
+import cases as C
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL_F32 = 1e-5
+
+
+@pytest.fixture(scope="module")
+def D():
+    from distributedmoellm_b200 import _build
+    _build.build()
+    from distributedmoellm_b200 import device
+    device.require_device()
+    return device
+
+
+def cu(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def row_err(got, want):
+    got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
+    return float((np.abs(got - want).max(axis=1) / np.maximum(np.abs(want).max(axis=1), 1e-30)).max())
+
+
+def same_bits(got, want):
+    fin = np.isfinite(want)
+    return (np.array_equal(np.isnan(got), np.isnan(want)) and np.array_equal(np.isinf(got), np.isinf(want))
+            and np.array_equal(got.view(np.uint32)[fin], want.view(np.uint32)[fin]))
+
+
+# ---- dequantisation ------------------------------------------------------------------
+
+@pytest.mark.parametrize("off", [0, 1])
+@pytest.mark.parametrize("f16", [False, True])
+def test_q4_dequant(D, golden, off, f16):
+    raw, s = C.q4_deq_inputs()
+    r = raw ^ 0x88 if off else raw
+    if f16:
+        s = s.astype(np.float16)
+        want = O.q4_dequant(r, s.astype(np.float32), 32, bool(off))
+    else:
+        want = golden[f"q4_deq_off{off}"]
+    got = D.q4_dequant(cu(r), cu(s), 32, bool(off)).cpu().numpy()
+    assert same_bits(got, want)
+
+
+def test_q8_dequant(D, golden):
+    q, s = C.q8_deq_inputs()
+    assert same_bits(D.q8_dequant(cu(q), cu(s), 32).cpu().numpy(), golden["q8_deq"])
+
+
+@pytest.mark.parametrize("qt", sorted(C.GGUF_BLOCK))
+def test_gguf_dequant_all_types(D, golden, qt):
+    raw = C.gguf_deq_inputs(qt)
+    got = D.gguf_dequant(cu(raw), qt, C.GGUF_COLS).cpu().numpy()
+    assert same_bits(got, golden[f"gguf_deq_{qt}"])
+
+
+def test_gguf_dequant_large(D):
+    rng = np.random.default_rng(3)
+    for qt in (12, 8, 14):
+        raw = C.gguf_random_rows(300, 4096, qt, rng)
+        got = D.gguf_dequant(cu(raw), qt, 4096).cpu().numpy()
+        assert same_bits(got, O.gguf_dequant(raw, qt, 4096))
+
+
+# ---- router, permute, combine --------------------------------------------------------
+
+def test_router_known_answer(D, golden):
+    idx, w = D.router_topk(cu(golden["router_known_logits"]), 2, True)
+    assert idx.cpu().numpy().tolist() == [[1, 3], [0, 3]]
+    np.testing.assert_allclose(w.cpu().numpy(), golden["router_known_w"], rtol=1e-6)
+
+
+@pytest.mark.parametrize("case", C.ROUTER_CASES, ids=[c[0] for c in C.ROUTER_CASES])
+def test_router_topk_matches_reference(D, golden, case):
+    name, T, E, k, norm, seed = case
+    lg = C.router_logits(T, E, seed)
+    idx, w = D.router_topk(cu(lg), k, norm)
+    idx, w = idx.cpu().numpy(), w.cpu().numpy()
+    ties = set(O.near_ties(lg, k).tolist())
+    rows = [t for t in range(T) if t not in ties]
+    assert len(ties) <= max(1, T // 50)
+    assert np.array_equal(idx[rows], golden[f"{name}_idx"][rows])
+    np.testing.assert_allclose(w[rows], golden[f"{name}_w"][rows], rtol=2e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("case", C.ROUTER_CASES, ids=[c[0] for c in C.ROUTER_CASES])
+def test_permute_matches_group_by_expert(D, golden, case):
+    name, T, E, k, norm, seed = case
+    idx, w = golden[f"{name}_idx"], golden[f"{name}_w"]
+    r = D.permute(cu(idx), cu(w), E)
+    torch.cuda.synchronize()
+    n = int(r.n_unique.item())
+    assert np.array_equal(r.uexperts[:n].cpu().numpy(), golden[f"{name}_experts"])
+    assert np.array_equal(r.uoffsets[:n + 1].cpu().numpy(), golden[f"{name}_offsets"])
+    assert np.array_equal(r.sorted_rows[:T * k].cpu().numpy(), golden[f"{name}_rows"])
+    assert np.array_equal(r.sorted_w[:T * k].cpu().numpy(), golden[f"{name}_weights"])
+    inv = r.inv[:T * k].cpu().numpy()
+    assert np.array_equal(np.sort(inv), np.arange(T * k))
+    counts = np.bincount(idx.reshape(-1), minlength=E)
+    assert np.array_equal(r.counts.cpu().numpy(), counts)
+
+
+def test_permute_large_and_skewed(D):
+    rng = np.random.default_rng(7)
+    T, k, E = 4096, 8, 128
+    idx = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+    idx[:1000, 0] = 5                      # a hot expert
+    idx[:1000, 1:] = np.arange(1, k)[None, :] + 10
+    w = rng.random((T, k), dtype=np.float32)
+    r = D.permute(cu(idx), cu(w), E)
+    ex, off, rows, wts = O.group_by_expert(idx, w)
+    torch.cuda.synchronize()
+    assert np.array_equal(r.sorted_rows.cpu().numpy(), rows)
+    assert np.array_equal(r.sorted_w.cpu().numpy(), wts)
+    assert int(r.n_unique.item()) == len(ex)
+
+
+def test_combine(D):
+    rng = np.random.default_rng(1)
+    T, k, H = 37, 3, 256
+    y = rng.standard_normal((T * k, H)).astype(np.float32)
+    inv = rng.permutation(T * k).astype(np.int32)
+    w = rng.random(T * k).astype(np.float32)
+    want = np.zeros((T, H), np.float32)
+    for t in range(T):
+        for j in range(k):
+            want[t] += w[t * k + j] * y[inv[t * k + j]]
+    got = D.combine(cu(y), cu(inv), cu(w), T, k).cpu().numpy()
+    assert row_err(got, want) < 1e-6
+    base = rng.standard_normal((T, H)).astype(np.float32)
+    out = cu(base)
+    D.combine(cu(y), cu(inv), cu(w), T, k, out=out, accumulate=True)
+    assert row_err(out.cpu().numpy(), want + base) < 1e-6
+
+
+# ---- single-matrix products from packed bytes ----------------------------------------
+
+@pytest.mark.parametrize("rows", C.MATMUL_ROWS)
+def test_q4_matmul_known_answer(D, golden, rows):
+    from distributedmoellm_b200 import layout as L
+    raw, s, W, x = C.q4_mm_inputs(rows)
+    tiles = cu(L.q4_tiles(raw, s, 32, False))
+    got = D.matmul_t(tiles, L.FMT_Q4_F32, 96, 128, cu(x)).cpu().numpy()
+    np.testing.assert_allclose(got, x @ W.T, atol=1e-3)
+    assert row_err(got, golden[f"q4_mm_{rows}"]) < TOL_F32
+
+
+@pytest.mark.parametrize("n", [1, 5, 9, 40])
+def test_q8_matmul(D, n):
+    from distributedmoellm_b200 import layout as L
+    rng = np.random.default_rng(n)
+    q = rng.integers(-127, 128, (200, 768), dtype=np.int8)
+    s = (rng.random((200, 24), dtype=np.float32) * 1e-3)
+    x = rng.standard_normal((n, 768)).astype(np.float32)
+    got = D.matmul_t(cu(L.q8_tiles(q, s, 32)), L.FMT_Q8_F32, 200, 768, cu(x)).cpu().numpy()
+    assert row_err(got, O.q8_matmul_t(x, q, s, 32)) < TOL_F32
+
+
+@pytest.mark.parametrize("rows", C.GGUF_MM_ROWS)
+def test_gguf_q8_0_and_q4_0_matmul(D, golden, rows):
+    from distributedmoellm_b200 import layout as L
+    raw, x = C.gguf_mm_inputs(8, rows)
+    q, d = L.q8_0_as_q8(raw, C.GGUF_COLS)
+    got = D.matmul_t(cu(L.q8_tiles(q, d, 32)), L.FMT_Q8_F16, raw.shape[0], C.GGUF_COLS, cu(x)).cpu().numpy()
+    assert row_err(got, golden[f"gguf_mm_8_{rows}"]) < TOL_F32
+    raw, x = C.gguf_mm_inputs(2, rows)
+    u, d = L.q4_0_as_q4(raw, C.GGUF_COLS)
+    got = D.matmul_t(cu(L.q4_tiles(u, d, 32, True)), L.FMT_Q4_F16, raw.shape[0], C.GGUF_COLS, cu(x)).cpu().numpy()
+    assert row_err(got, golden[f"gguf_mm_2_{rows}"]) < TOL_F32
+
+
+# ---- one MoE layer ------------------------------------------------------------------
+
+def _layer(cfg, kind, experts, router, f16=False):
+    from distributedmoellm_b200 import layout as L
+    from distributedmoellm_b200.layer import MoELayer
+    from distributedmoellm_b200.store import LayerExperts
+    H, I, E = cfg["H"], cfg["I"], cfg["E"]
+    if kind == "q4":
+        s0 = experts[0][1].astype(np.float16) if f16 else experts[0][1]
+        fmt = L.fmt_of("q4", s0)
+    else:
+        fmt = L.FMT_Q8_F32
+    ex = LayerExperts(E, H, I, cfg["gs"], fmt, fmt, "cuda")
+    for e, parts in experts.items():
+        if kind == "q4":
+            gr, gsc, dr, dsc = parts
+            if f16:
+                gsc, dsc = gsc.astype(np.float16), dsc.astype(np.float16)
+            ex.put_int4(e, gr, gsc, dr, dsc, offset=False)
+        else:
+            ex.put_int8(e, *parts)
+    ex.publish()
+    return MoELayer(cu(router), ex, cfg["k"], True)
+
+
+def test_layer_int4_matches_reference(D, golden):
+    x, router, experts = C.layer_inputs(C.LAYER, "int4")
+    layer = _layer(C.LAYER, "q4", experts, router)
+    out = layer(cu(x)).cpu().numpy()
+    b = layer.buffers(x.shape[0])
+    ties = set(O.near_ties(golden["layer_q4_logits"], 2).tolist())
+    rows = [t for t in range(x.shape[0]) if t not in ties]
+    assert np.array_equal(b.idx.cpu().numpy()[rows], golden["layer_q4_idx"][rows])
+    assert row_err(out[rows], golden["layer_q4_out"][rows]) < TOL_F32
+    assert layer.status(x.shape[0]) == 0
+
+
+def test_layer_int4_f16_scales_matches_reference(D, golden):
+    x, router, experts = C.layer_inputs(C.LAYER_F16, "int4", f16_scales=True)
+    layer = _layer(C.LAYER_F16, "q4", experts, router, f16=True)
+    out = layer(cu(x)).cpu().numpy()
+    assert np.array_equal(layer.buffers(x.shape[0]).idx.cpu().numpy(), golden["layer_q4h_idx"])
+    assert row_err(out, golden["layer_q4h_out"]) < TOL_F32
+
+
+def test_layer_int8_matches_reference(D, golden):
+    x, router, experts = C.layer_inputs(C.LAYER_Q8, "int8")
+    layer = _layer(C.LAYER_Q8, "q8", experts, router)
+    out = layer(cu(x)).cpu().numpy()
+    assert np.array_equal(layer.buffers(x.shape[0]).idx.cpu().numpy(), golden["layer_q8_idx"])
+    assert row_err(out, golden["layer_q8_out"]) < TOL_F32
+
+
+@pytest.fixture(scope="module")
+def qwen_layer(D):
+    """Config 2: Qwen3-30B-A3B MoE layer shape, int4 g32 with f16 scales."""
+    from distributedmoellm_b200 import synthetic as S
+    rng = np.random.default_rng(0)
+    H, I, E, k, gs = 2048, 768, 128, 8, 32
+    experts = {e: S.int4_expert(rng, H, I, gs, f16_scales=True) for e in range(E)}
+    router = S.router(rng, E, H)
+    cfg = dict(H=H, I=I, E=E, k=k, gs=gs)
+    layer = _layer(cfg, "q4", experts, router, f16=True)
+    desc = {e: (("q4", gr, gsc.astype(np.float32), gs, False), ("q4", dr, dsc.astype(np.float32), gs, False))
+            for e, (gr, gsc, dr, dsc) in experts.items()}
+    return layer, desc, router, cfg
+
+
+@pytest.mark.parametrize("T", [1, 8, 32, 64])
+def test_qwen_shape_decode_matches_oracle(qwen_layer, T):
+    layer, desc, router, cfg = qwen_layer
+    from distributedmoellm_b200 import synthetic as S
+    x = S.hidden(np.random.default_rng(100 + T), T, cfg["H"])
+    out = layer(cu(x)).cpu().numpy()
+    b = layer.buffers(T)
+    idx, w = b.idx.cpu().numpy(), b.w.cpu().numpy()
+    ex, off, rows, wts = O.group_by_expert(idx, w)
+    groups = [(ex[i], rows[off[i]:off[i + 1]], wts[off[i]:off[i + 1]]) for i in range(len(ex))]
+    want = O.store_compute(x, groups, desc, cfg["I"])
+    assert row_err(out, want) < TOL_F32
+    # and the router against the oracle's on the GPU's own logits
+    ridx, rw = O.route(b.logits.cpu().numpy(), cfg["k"], True)
+    ties = set(O.near_ties(b.logits.cpu().numpy(), cfg["k"]).tolist())
+    keep = [t for t in range(T) if t not in ties]
+    assert np.array_equal(idx[keep], ridx[keep])
+    assert layer.status(T) == 0
+
+
+def test_bad_format_raises(D):
+    from distributedmoellm_b200 import _lib
+    t = torch.zeros(1024, dtype=torch.uint8, device="cuda")
+    x = torch.zeros((2, 128), dtype=torch.float32, device="cuda")
+    with pytest.raises(RuntimeError, match="weight format"):
+        D.matmul_t(t, 99, 16, 128, x)
+    assert "weight format" in _lib.last_error()
