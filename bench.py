@@ -43,12 +43,14 @@ L2_ROTATE_LAYERS = 4
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--steps", type=int, default=400)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--tokens", type=int, default=64)
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--profile", action="store_true",
+                   help="only the main timed loop (for ncu): no e2e, sweep or CPU baseline")
     return p.parse_args()
 
 
@@ -70,45 +72,49 @@ def make_experts(seed=0):
 # ---- clocks sampled during the timed region ------------------------------------------
 
 class Clocks:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock, power and clock-event reasons sampled through NVML (what
+    nvidia-smi reads) every few ms while the timed region runs."""
 
-    def __init__(self, gpu_index: int):
-        self.idx, self.rows, self.proc = gpu_index, [], None
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, gpu_index: int, period_s: float = 0.005):
+        self.idx, self.period, self.rows, self.stop, self.t = gpu_index, period_s, [], threading.Event(), None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml as N
+            N.nvmlInit()
+            h = N.nvmlDeviceGetHandleByIndex(self.idx)
+            self.max_sm = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+
+            def poll():
+                while not self.stop.is_set():
+                    try:
+                        self.rows.append((N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM),
+                                          N.nvmlDeviceGetCurrentClocksEventReasons(h),
+                                          N.nvmlDeviceGetPowerUsage(h) / 1000.0))
+                    except Exception:
+                        pass
+                    time.sleep(self.period)
+            self.t = threading.Thread(target=poll, daemon=True)
             self.t.start()
         except Exception:
-            self.proc = None
+            self.max_sm = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([v.strip() for v in line.split(",")])
-
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self.stop.set()
+        if self.t is not None:
+            self.t.join(timeout=2)
 
     def summary(self):
         if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 5 + i and r[5 + i] == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+            return {"sm_mhz": None, "sm_max_mhz": self.max_sm, "reasons": ["unsampled"], "samples": 0}
+        reasons = sorted({n for _, r, _ in self.rows for n, bit in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": self.max_sm,
+                "reasons": reasons, "samples": len(self.rows),
+                "power_w_max": round(max(r[2] for r in self.rows), 1)}
 
 
 # ---- CPU side: the reference's algorithm (oracle restatement) -----------------------------
@@ -167,41 +173,38 @@ def run_gpu(args, rank, world, dev):
     layers = build_layers(experts, router, dev, L2_ROTATE_LAYERS)
     pk, pk_kind = peaks()
 
-    def measure(T, steps, warmup, decode_events=True):
+    def measure(T, steps, warmup):
+        """Step time (graph replays of the whole layer) and expert-kernel time
+        (graph replays of the decode kernels alone), both by CUDA events."""
         rng = np.random.default_rng(1000 + 17 * rank + T)
         xs = [torch.from_numpy(rng.standard_normal((T, H), dtype=np.float32)).to(dev) for _ in range(len(layers))]
-        # unique experts of each (layer, batch) pair, for the algorithmic bytes
-        uniq = []
-        for l, x in zip(layers, xs):
-            b = l.route(x)
-            torch.cuda.synchronize()
-            uniq.append(int(b.routing.n_unique.item()))
+        full = [l.capture(x) for l, x in zip(layers, xs)]
+        dec = [l.capture(x, experts_only=True) for l, x in zip(layers, xs)]
+        torch.cuda.synchronize()
+        uniq = [int(l.buffers(T).routing.n_unique.item()) for l in layers]
+        L = len(layers)
         for i in range(warmup):
-            layers[i % len(layers)](xs[i % len(layers)])
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record()
-        for i in range(steps):
-            l = layers[i % len(layers)]
-            x = xs[i % len(layers)]
-            b = l.route(x)
-            if decode_events:
-                ev[i][0].record()
-            l.experts_forward(x, b)
-            if decode_events:
-                ev[i][1].record()
-            D.combine(b.y, b.routing.inv, b.w.view(-1), T, K_TOP, out=b.out)
-        stop.record()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        ms = start.elapsed_time(stop) / steps
-        dec_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev) if decode_events else None
-        u_avg = statistics.mean(uniq[i % len(layers)] for i in range(steps))
+            full[i % L].replay()
+
+        def timed(graphs):
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for i in range(steps):
+                graphs[i % L].replay()
+            b.record()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            return a.elapsed_time(b) / steps
+
+        ms = timed(full)
+        dec_ms = timed(dec)
+        u_avg = statistics.mean(uniq[i % L] for i in range(steps))
         status = max(int(l.status(T)) for l in layers)
+        del full, dec
         return ms, dec_ms, u_avg, status
 
     def max_over_ranks(v):
@@ -212,8 +215,12 @@ def run_gpu(args, rank, world, dev):
         return float(t.item())
 
     T = args.tokens
-    with Clocks(int(str(dev).split(":")[-1]) if ":" in str(dev) else 0) as clk:
+    gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(dev.index or 0)).split(",")[dev.index or 0]) \
+        if os.environ.get("CUDA_VISIBLE_DEVICES", "").replace(",", "").isdigit() else (dev.index or 0)
+    with Clocks(gpu_index) as clk:
         ms, dec_ms, u_avg, status = measure(T, args.steps, args.warmup)
+    if args.profile:
+        return world * T / (ms / 1e3), ms, {}, {}, {}, None, clk.summary(), status
     ms = max_over_ranks(ms)
     value = world * T / (ms / 1e3)
 
@@ -253,19 +260,26 @@ def run_gpu(args, rank, world, dev):
 
 
 def measure_e2e(layers, T, steps, warmup, world, dev):
+    """The same step through the public API with host buffers: per step the
+    inputs are copied from pinned host memory, the layer runs (its CUDA graph)
+    and the output is read back to pinned host memory, all inside the timed
+    region."""
     import torch
     import torch.distributed as dist
     rng = np.random.default_rng(999)
     hx = [torch.from_numpy(rng.standard_normal((T, H), dtype=np.float32)).pin_memory() for _ in layers]
     hout = torch.empty((T, H), dtype=torch.float32).pin_memory()
     dx = [torch.empty((T, H), dtype=torch.float32, device=dev) for _ in layers]
+    for x, h in zip(dx, hx):
+        x.copy_(h)
+    graphs = [l.capture(x) for l, x in zip(layers, dx)]
+    outs = [l.buffers(T).out for l in layers]
+    L = len(layers)
 
     def step(i):
-        l = layers[i % len(layers)]
-        x = dx[i % len(layers)]
-        x.copy_(hx[i % len(layers)], non_blocking=True)
-        out = l(x)
-        hout.copy_(out, non_blocking=True)
+        dx[i % L].copy_(hx[i % L], non_blocking=True)
+        graphs[i % L].replay()
+        hout.copy_(outs[i % L], non_blocking=True)
 
     for i in range(warmup):
         step(i)
@@ -279,7 +293,7 @@ def measure_e2e(layers, T, steps, warmup, world, dev):
     b.record()
     torch.cuda.synchronize()
     return {"ms": a.elapsed_time(b) / steps, "unit": UNIT, "h2d_bytes_per_step": T * H * 4,
-            "d2h_bytes_per_step": T * H * 4, "api": "distributedmoellm_b200.layer.MoELayer.forward"}
+            "d2h_bytes_per_step": T * H * 4, "api": "distributedmoellm_b200.layer.MoELayer (CUDA graph of forward)"}
 
 
 def run_reference(args):

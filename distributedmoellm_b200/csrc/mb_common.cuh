@@ -83,6 +83,19 @@ __device__ __forceinline__ bool mb_mbar_try_wait(uint64_t* bar, uint32_t parity)
     return ok != 0;
 }
 
+// try_wait that may park the thread in hardware for up to `ns` nanoseconds
+// (woken early when the phase completes), so waiting warps issue nothing.
+__device__ __forceinline__ bool mb_mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(mb_smem_addr(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for phase `parity` of `bar` to complete, for at most MB_WAIT_LIMIT_NS.
 // On time-out sets MB_STATUS_TIMEOUT in *status and *abort_flag and returns false.
 // Once *abort_flag is set (by any thread of the CTA) it returns false at once.
@@ -90,12 +103,20 @@ __device__ __forceinline__ bool mb_mbar_wait(uint64_t* bar, uint32_t parity, uns
                                              volatile int* abort_flag)
 {
     if (mb_mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = mb_globaltimer();
-    for (uint32_t i = 1;; ++i) {
+    // back off with __nanosleep so waiting warps leave the issue slots (and the
+    // special-register pipe) to the warps doing work; read the timer rarely
+    uint64_t t0 = 0;
+    uint32_t ns = 20;
+    for (uint32_t i = 0;; ++i) {
+        __nanosleep(ns);
+        if (ns < 320) ns <<= 1;
         if (mb_mbar_try_wait(bar, parity)) return true;
-        if ((i & 63u) == 0) {
+        if ((i & 15u) == 15u) {
             if (*abort_flag) return false;
-            if (mb_globaltimer() - t0 > MB_WAIT_LIMIT_NS) {
+            const uint64_t now = mb_globaltimer();
+            if (t0 == 0) {
+                t0 = now;
+            } else if (now - t0 > MB_WAIT_LIMIT_NS) {
                 atomicOr(status, MB_STATUS_TIMEOUT);
                 *abort_flag = 1;
                 return false;
@@ -137,15 +158,26 @@ __device__ __forceinline__ float mb_f16_ref(uint32_t h)
     return (h & 0x8000) ? -v : v;
 }
 
-// mma.sync m16n8k16, f16 x f16 -> f32, D = A*B + C.
+// mma.sync m16n8k16, f16 x f16 -> f32, accumulating in place: D += A*B.
+// (No volatile: independent MMAs may be interleaved by the compiler.)
 __device__ __forceinline__ void mb_mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                           uint32_t b0, uint32_t b1, const float (&c)[4])
+                                           uint32_t b0, uint32_t b1)
 {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%10,%11,%12,%13};"
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// D = A*B (zero accumulator).
+__device__ __forceinline__ void mb_mma_f16_zero(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                uint32_t b0, uint32_t b1)
+{
+    const float z = 0.0f;
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
         : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
 }
 
 __device__ __forceinline__ uint32_t mb_lop_and_or(uint32_t a, uint32_t mask, uint32_t orv)

@@ -7,36 +7,41 @@
 // Design (sm_100a):
 //  * Weights live in the device tile layout: 16-row tiles, each a contiguous
 //    run of 1 KB (int4) / 2 KB (int8) blocks of 128 columns plus the blocks'
-//    group scales.  One producer warp streams a row tile per stage into a
-//    shared-memory ring with 1-D bulk copies on the TMA engine (mbarrier
-//    completion); the whole working set moves HBM -> SMEM exactly once.
-//  * Consumer warps split K: warp w owns quads [w*QPW, w*QPW+QPW) of every
-//    tile.  Weights are unpacked to exact f16 (values -8..7 / -128..127) with
+//    group scales.  One producer warp streams MT consecutive tiles per stage
+//    (~30 KB) into a shared-memory ring with 1-D bulk copies on the TMA engine
+//    (mbarrier completion); the working set moves HBM -> SMEM exactly once.
+//  * MMA warps split K: warp w owns quad w (128 columns) of every tile.
+//    Weights are unpacked to exact f16 (values -8..7 / -128..127) with
 //    lop3/prmt + one f16x2 op per pair, and multiplied on the tensor cores by
 //    mma.sync m16n8k16 against the activations split into two f16 pieces
-//    (x * 2^e = hi + lo, 22 significant bits) laid along K, with f32
+//    (x * 2^e = hi + lo, 22 significant bits) laid along N, with f32
 //    accumulation: the products are exact, so results match an f32 mat-vec to
 //    rounding.  mma.sync is used because its operands come from registers:
-//    a decode mat-vec is bound by HBM, and this keeps the unpacked weights
-//    out of shared memory entirely (tcgen05 would need them staged).
+//    a decode mat-vec is bound by HBM, and this keeps the unpacked weights out
+//    of shared memory entirely (tcgen05 would need them staged there).
 //  * Each group of 32 columns is accumulated separately and scaled by its
-//    group scale in f32; K-split partials are summed through shared memory.
+//    group scale in f32; the K-split partials go through shared-memory
+//    reduction buffers (mbarrier hand-off) to two epilogue warps, which sum
+//    them with 128-bit loads.
 //  * Phase 1 (gate|up) tiles interleave 8 gate rows with the 8 matching up
 //    rows, so SiLU(gate) * up is formed in the epilogue and only the
 //    activation row (P x I) goes back to HBM, with each pick's max |act|.
 //  * Phase 2 (down) writes each pick's unweighted output row; the weighted
 //    combine is a separate deterministic kernel.
-//  * Work items are (expert, chunk of 8 picks, row tile), split contiguously
-//    over a persistent grid so each CTA touches one or two experts.
+//  * Work items are (expert, chunk of 8 picks, MT row tiles), split
+//    contiguously over a persistent grid so each CTA touches one or two
+//    experts.
 #include <type_traits>
 
 #include "mb_common.cuh"
 
 namespace {
 
-constexpr int kMaxQPW = 2;         // quads (128 columns) per consumer warp
-constexpr int kMaxKW = 8;          // consumer warps
-constexpr int kThreadsMax = (kMaxKW + 1) * 32;
+constexpr int kMaxKW = 16;      // MMA warps: one per quad (128 columns) of K, so K <= 2048
+constexpr int kEpiWarps = 2;    // epilogue warps, taking alternate items
+constexpr int kThreadsMax = (kMaxKW + 1 + kEpiWarps) * 32;
+constexpr int kMaxMT = 4;       // row tiles per stage
+constexpr int kRedTile = 128;   // floats of one warp's partial of one tile: [8 input rows][16 rows]
 
 struct Fmt {
     int data_bytes;   // per block: 1024 (int4) or 2048 (int8)
@@ -60,12 +65,13 @@ struct DecodeArgs {
     int K;            // real input columns
     int NQ;           // quads per tile row (K padded to 128)
     int RT;           // row tiles
+    int MT;           // row tiles per stage
     int O_real;       // phase 1: I (act columns), phase 2: H (y columns)
     int src_ld;       // floats per input row (x: H, act: I_pad)
     int act_ld;       // I_pad
     int y_ld;         // H
-    int QPW, KW;
-    int stages, stage_bytes;
+    int KW;           // MMA warps (= NQ)
+    int stages, tile_bytes, nred;
     const int32_t* counts;
     const int32_t* offsets;
     const int32_t* sorted_rows;
@@ -82,24 +88,9 @@ struct DecodeArgs {
     int single_n;
 };
 
-__device__ __forceinline__ int items_of(int n, int max_rows, int RT)
+__device__ __forceinline__ int64_t items_of(int n, int max_rows, int RTS)
 {
-    return (n > 0 && n <= max_rows) ? ((n + 7) >> 3) * RT : 0;
-}
-
-// item -> (expert, chunk, row tile) by binary search over the item prefix.
-__device__ __forceinline__ void locate(const int64_t* pre, int E, int RT, int64_t item, int& e, int& c, int& rt)
-{
-    int lo = 0, hi = E;  // pre[lo] <= item < pre[hi]
-    while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (pre[mid] <= item) lo = mid;
-        else hi = mid;
-    }
-    e = lo;
-    const int rem = (int)(item - pre[lo]);
-    c = rem / RT;
-    rt = rem - c * RT;
+    return (n > 0 && n <= max_rows) ? (int64_t)((n + 7) >> 3) * RTS : 0;
 }
 
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
@@ -127,18 +118,18 @@ __device__ __forceinline__ void unpack_q8(uint32_t w0, uint32_t w1, uint32_t (&p
     p[3] = mb_hsub2(mb_prmt(w1, kHi, 0x4342u), kSub);
 }
 
-template <bool Q8, bool F16S>
-__device__ __forceinline__ void scales4(const uint8_t* blk, int data_bytes, int row, float (&s)[4])
+template <bool F16S>
+__device__ __forceinline__ void scales4(const uint8_t* p, float (&s)[4])
 {
     if (F16S) {
-        const uint2 v = *reinterpret_cast<const uint2*>(blk + data_bytes + row * 8);
+        const uint2 v = *reinterpret_cast<const uint2*>(p);
         const __half2 a = *reinterpret_cast<const __half2*>(&v.x), b = *reinterpret_cast<const __half2*>(&v.y);
         s[0] = __low2float(a);
         s[1] = __high2float(a);
         s[2] = __low2float(b);
         s[3] = __high2float(b);
     } else {
-        const float4 v = *reinterpret_cast<const float4*>(blk + data_bytes + row * 16);
+        const float4 v = *reinterpret_cast<const float4*>(p);
         s[0] = v.x;
         s[1] = v.y;
         s[2] = v.z;
@@ -146,263 +137,394 @@ __device__ __forceinline__ void scales4(const uint8_t* blk, int data_bytes, int 
     }
 }
 
-template <int FMT>
-__global__ void __launch_bounds__(kThreadsMax, 1) moe_decode_kernel(const DecodeArgs a)
+// Work-item cursor over (expert, chunk of 8 picks, stage of MT row tiles).
+struct ItemCursor {
+    int e, c, sg;
+    __device__ __forceinline__ void start(const int64_t* pre, int E, int RTS, int64_t item)
+    {
+        int lo = 0, hi = E;  // pre[lo] <= item < pre[hi]
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (pre[mid] <= item) lo = mid;
+            else hi = mid;
+        }
+        e = lo;
+        const int rem = (int)(item - pre[lo]);
+        c = rem / RTS;
+        sg = rem - c * RTS;
+    }
+    __device__ __forceinline__ void next(const int64_t* pre, int E, int RTS)
+    {
+        if (++sg < RTS) return;
+        sg = 0;
+        if ((int64_t)(++c) * RTS < pre[e + 1] - pre[e]) return;
+        c = 0;
+        do {
+            ++e;
+        } while (e < E - 1 && pre[e + 1] == pre[e]);
+    }
+};
+
+// Warp roles: [0, KW) MMA warps (warp w owns quads QPW*w .. QPW*w+QPW-1 of K), KW the TMA
+// producer, KW+1 and KW+2 the epilogue (even and odd items).  Shared memory:
+// weight stages | reduction buffers [nred][KW][MT][8][16] | mbarriers | item
+// prefix | abort flag.
+// largest block of an instantiation: 16 MMA warps with one quad each, 8 with two
+constexpr int threads_max(int qpw) { return ((qpw == 2 ? kMaxKW / 2 : kMaxKW) + 1 + kEpiWarps) * 32; }
+
+template <int FMT, int QPW>
+__global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const __grid_constant__ DecodeArgs a)
 {
     constexpr bool Q8 = (FMT == MB_FMT_Q8_F16 || FMT == MB_FMT_Q8_F32);
     constexpr bool F16S = (FMT == MB_FMT_Q4_F16 || FMT == MB_FMT_Q8_F16);
     constexpr int kData = Q8 ? 2048 : 1024;
     constexpr int kBlock = kData + 16 * 4 * (F16S ? 2 : 4);
 
+    const int S = a.stages, KW = a.KW, E = a.E, RT = a.RT, MT = a.MT, NR = a.nred;
+    const int RTS = (RT + MT - 1) / MT;
+    const int tile_bytes = a.tile_bytes, stage_bytes = MT * tile_bytes;
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* stages = smem;
-    float* red = reinterpret_cast<float*>(smem + (size_t)a.stages * a.stage_bytes);  // [2][KW][16][8]
-    uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * a.KW * 128);
-    uint64_t* empty = full + a.stages;
-    int64_t* pre = reinterpret_cast<int64_t*>(empty + a.stages);                      // [E+1]
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(pre + a.E + 1);
+    float* red = reinterpret_cast<float*>(smem + (size_t)S * stage_bytes);
+    const int red_buf = KW * MT * kRedTile;  // floats per reduction buffer
+    uint64_t* full = reinterpret_cast<uint64_t*>(red + NR * red_buf);
+    uint64_t* empty = full + S;
+    uint64_t* rfull = empty + S;
+    uint64_t* rempty = rfull + NR;
+    int64_t* pre = reinterpret_cast<int64_t*>(rempty + NR);  // [E+1]
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(pre + E + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int nthr = a.KW * 32;
 
-    // ---- item prefix over experts (warp 0), barriers (thread 0)
-    if (warp == 0) {
+    if (warp == 0) {  // items per expert -> prefix
         int64_t run = 0;
-        for (int base = 0; base < a.E; base += 32) {
+        for (int base = 0; base < E; base += 32) {
             const int e = base + lane;
             int64_t v = 0;
-            if (e < a.E) v = items_of(a.single_n ? (e == 0 ? a.single_n : 0) : a.counts[e], a.max_rows, a.RT);
+            if (e < E) v = items_of(a.single_n ? (e == 0 ? a.single_n : 0) : a.counts[e], a.max_rows, RTS);
             for (int o = 1; o < 32; o <<= 1) {
                 const int64_t u = __shfl_up_sync(0xffffffffu, v, o);
                 if (lane >= o) v += u;
             }
-            if (e < a.E) pre[e + 1] = run + v;
+            if (e < E) pre[e + 1] = run + v;
             run += __shfl_sync(0xffffffffu, v, 31);
         }
         if (lane == 0) pre[0] = 0;
     }
     if (tid == 0) {
-        for (int s = 0; s < a.stages; ++s) {
-            mb_mbar_init(&full[s], 1);
-            mb_mbar_init(&empty[s], a.KW);
+        for (int i = 0; i < S; ++i) {
+            mb_mbar_init(&full[i], 1);
+            mb_mbar_init(&empty[i], KW);
+        }
+        for (int i = 0; i < NR; ++i) {
+            mb_mbar_init(&rfull[i], KW);
+            mb_mbar_init(&rempty[i], 1);  // the epilogue warp that took the item
         }
         *abort_flag = 0;
         mb_fence_mbar_init();
     }
     __syncthreads();
 
-    const int64_t total = pre[a.E];
+    const int64_t total = pre[E];
     const int64_t lo = total * blockIdx.x / gridDim.x, hi = total * (blockIdx.x + 1) / gridDim.x;
+    if (lo >= hi) return;
+    const int64_t n_items = hi - lo;
+    ItemCursor cur;
+    cur.start(pre, E, RTS, lo);
 
-    if (warp == a.KW) {  // ---------------- producer
+    // ------------------------------------------------------------- producer
+    if (warp == KW) {
         if (lane == 0) {
-            int64_t it = 0;
-            for (int64_t item = lo; item < hi; ++item, ++it) {
-                const int s = (int)(it % a.stages);
-                const int64_t use = it / a.stages;
-                if (use > 0 && !mb_mbar_wait(&empty[s], (uint32_t)((use - 1) & 1), a.status, abort_flag)) break;
-                int e, c, rt;
-                locate(pre, a.E, a.RT, item, e, c, rt);
-                const void* wbase = a.single_w ? a.single_w : (a.phase == 1 ? a.table[e].gu : a.table[e].down);
-                const uint8_t* src = reinterpret_cast<const uint8_t*>(wbase) + (int64_t)rt * a.stage_bytes;
-                mb_mbar_arrive_expect_tx(&full[s], (uint32_t)a.stage_bytes);
-                mb_bulk_g2s(stages + (size_t)s * a.stage_bytes, src, (uint32_t)a.stage_bytes, &full[s]);
+            int s = 0;
+            uint32_t ph = 0;
+            int we = -1;
+            const uint8_t* wbase = nullptr;
+            for (int64_t it = 0; it < n_items; ++it, cur.next(pre, E, RTS)) {
+                if (it >= S && !mb_mbar_wait(&empty[s], ph ^ 1u, a.status, abort_flag)) break;
+                if (cur.e != we) {
+                    we = cur.e;
+                    wbase = reinterpret_cast<const uint8_t*>(
+                        a.single_w ? a.single_w : (a.phase == 1 ? a.table[we].gu : a.table[we].down));
+                }
+                const int nt = min(MT, RT - cur.sg * MT);
+                const uint32_t bytes = (uint32_t)(nt * tile_bytes);
+                mb_mbar_arrive_expect_tx(&full[s], bytes);
+                mb_bulk_g2s(stages + (size_t)s * stage_bytes, wbase + (int64_t)cur.sg * MT * tile_bytes, bytes,
+                            &full[s]);
+                if (++s == S) {
+                    s = 0;
+                    ph ^= 1u;
+                }
             }
         }
         return;
     }
 
-    // ---------------- consumers
-    const int q0 = warp * a.QPW;
-    const int nq = max(0, min(a.QPW, a.NQ - q0));
-    uint32_t bf[kMaxQPW][4][4][2];
-    // 2^-e of the input rows this thread's epilogue outputs belong to:
-    // phase 1 -> row (tid % 8); phase 2 -> row (o >> 4) of outputs o = tid + m * nthr
-    float fs[4];
-    int cur_e = -1, cur_c = -1, pbase = 0, nvalid = 0;
-    float rmax = 0.0f;     // phase 1: running max |act| of this thread's pick (n = tid % 8)
-    int64_t it = 0;
-
-    auto row_exp_of = [&](int n) -> int {
-        if (n >= nvalid) return 0;
-        if (a.phase == 1) return a.row_exp[a.sorted_rows[pbase + n]];
-        return mb_row_exponent(__uint_as_float(a.act_max[pbase + n]));
-    };
-    auto flush_max = [&]() {
-        if (a.phase != 1 || cur_e < 0) return;
-        float m = rmax;
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
-        const int n = tid & 7;
-        if (lane < 8 && tid < 64 && n < nvalid) atomicMax(&a.act_max[pbase + n], __float_as_uint(m));
-        rmax = 0.0f;
-    };
-
-    for (int64_t item = lo; item < hi; ++item, ++it) {
-        int e, c, rt;
-        locate(pre, a.E, a.RT, item, e, c, rt);
-        if (e != cur_e || c != cur_c) {
-            flush_max();
-            cur_e = e;
-            cur_c = c;
-            const int n_e = a.single_n ? a.single_n : a.counts[e];
-            pbase = (a.single_n ? 0 : a.offsets[e]) + 8 * c;
-            nvalid = min(8, n_e - 8 * c);
-            if (a.phase == 1) {
-                fs[0] = pow2f(-row_exp_of(tid & 7));
-            } else {
-#pragma unroll
-                for (int m = 0; m < 4; ++m) fs[m] = pow2f(-row_exp_of(min(7, (tid + m * nthr) >> 4)));
+    // ------------------------------------------------------------- epilogue
+    if (warp > KW) {
+        const int which = warp - KW - 1;    // items it with it % kEpiWarps == which
+        const int n = lane >> 2, rg = lane & 3;  // this lane: input row n, tile rows 4rg..4rg+3
+        int ke = -1, kc = -1, pbase = 0, nvalid = 0;
+        float fs = 1.f;     // 2^-e of input row n
+        float rmax = 0.f;   // phase 1: running max |act| of input row n
+        int r = which;
+        uint32_t rph = 0;
+        auto flush = [&]() {
+            float m = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 1));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+            if (rg == 0 && n < nvalid) atomicMax(&a.act_max[pbase + n], __float_as_uint(m));
+            rmax = 0.f;
+        };
+        for (int64_t it = 0; it < n_items; ++it, cur.next(pre, E, RTS)) {
+            if ((int)(it & (kEpiWarps - 1)) != which) continue;
+            if (cur.e != ke || cur.c != kc) {
+                if (a.phase == 1 && ke >= 0) flush();
+                ke = cur.e;
+                kc = cur.c;
+                pbase = (a.single_n ? 0 : a.offsets[ke]) + 8 * kc;
+                nvalid = min(8, (a.single_n ? a.single_n : a.counts[ke]) - 8 * kc);
+                int ex = 0;
+                if (n < nvalid) {
+                    if (a.phase == 1) ex = a.row_exp[a.sorted_rows[pbase + n]];
+                    else ex = mb_row_exponent(__uint_as_float(a.act_max[pbase + n]));
+                }
+                fs = pow2f(-ex);
             }
-            // B fragments: input row n = g of the chunk, split into f16 hi/lo of x * 2^e
-            const bool valid = g < nvalid;
-            const float* src = nullptr;
-            float up = 1.0f;
-            if (valid) {
-                if (a.phase == 1) src = a.x + (int64_t)a.sorted_rows[pbase + g] * a.src_ld;
-                else src = a.act + (int64_t)(pbase + g) * a.src_ld;
-                up = pow2f(row_exp_of(g));
-            }
-#pragma unroll
-            for (int qi = 0; qi < kMaxQPW; ++qi) {
-#pragma unroll
-                for (int gi = 0; gi < 4; ++gi) {
-                    float v[8];
-                    const int col0 = ((q0 + qi) * 4 + gi) * 32 + 8 * t;
-                    if (valid && qi < nq && col0 + 8 <= a.K) {
-                        const float4 u0 = *reinterpret_cast<const float4*>(src + col0);
-                        const float4 u1 = *reinterpret_cast<const float4*>(src + col0 + 4);
-                        v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
-                        v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            v[j] = (valid && qi < nq && col0 + j < a.K) ? src[col0 + j] : 0.0f;
+            const bool ok = mb_mbar_wait(&rfull[r], rph, a.status, abort_flag);
+            const int nt = min(MT, RT - cur.sg * MT);
+            if (ok) {
+                const float* rr = red + r * red_buf;
+                for (int mt = 0; mt < nt; ++mt) {
+                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int w = 0; w < KW; ++w) {
+                        const float4 u = *reinterpret_cast<const float4*>(rr + (w * MT + mt) * kRedTile + n * 16 + 4 * rg);
+                        v.x += u.x;
+                        v.y += u.y;
+                        v.z += u.z;
+                        v.w += u.w;
                     }
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float xa = v[j] * up, xb = v[j + 4] * up;
-                        const __half ha = __float2half_rn(xa), hb = __float2half_rn(xb);
-                        const __half la = __float2half_rn(xa - __half2float(ha));
-                        const __half lb = __float2half_rn(xb - __half2float(hb));
-                        bf[qi][gi][j][0] = mb_pack_h2(ha, hb);
-                        bf[qi][gi][j][1] = mb_pack_h2(la, lb);
+                    const int rt = cur.sg * MT + mt;
+                    if (a.phase == 1) {
+                        // lanes rg 0,1 hold gate rows 4rg..4rg+3, lanes rg 2,3 the matching up rows
+                        const float ux = __shfl_down_sync(0xffffffffu, v.x, 2), uy = __shfl_down_sync(0xffffffffu, v.y, 2);
+                        const float uz = __shfl_down_sync(0xffffffffu, v.z, 2), uw = __shfl_down_sync(0xffffffffu, v.w, 2);
+                        if (rg < 2 && n < nvalid) {
+                            float4 o;
+                            float gg;
+                            gg = v.x * fs; o.x = gg / (1.0f + expf(-gg)) * (ux * fs);
+                            gg = v.y * fs; o.y = gg / (1.0f + expf(-gg)) * (uy * fs);
+                            gg = v.z * fs; o.z = gg / (1.0f + expf(-gg)) * (uz * fs);
+                            gg = v.w * fs; o.w = gg / (1.0f + expf(-gg)) * (uw * fs);
+                            *reinterpret_cast<float4*>(a.act + (int64_t)(pbase + n) * a.act_ld + 8 * rt + 4 * rg) = o;
+                            rmax = fmaxf(rmax, fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w))));
+                        }
+                    } else if (n < nvalid) {
+                        const int orow = 16 * rt + 4 * rg;
+                        float* dst = a.y + (int64_t)(pbase + n) * a.y_ld + orow;
+                        const float4 o = make_float4(v.x * fs, v.y * fs, v.z * fs, v.w * fs);
+                        if (orow + 4 <= a.O_real) {
+                            *reinterpret_cast<float4*>(dst) = o;
+                        } else {
+                            if (orow < a.O_real) dst[0] = o.x;
+                            if (orow + 1 < a.O_real) dst[1] = o.y;
+                            if (orow + 2 < a.O_real) dst[2] = o.z;
+                        }
                     }
                 }
             }
+            __syncwarp();
+            if (lane == 0) mb_mbar_arrive(&rempty[r]);
+            r += kEpiWarps;
+            if (r >= NR) {
+                r -= NR;
+                rph ^= 1u;
+            }
         }
+        if (a.phase == 1 && ke >= 0) flush();
+        return;
+    }
 
-        const int s = (int)(it % a.stages);
-        const bool ok = mb_mbar_wait(&full[s], (uint32_t)((it / a.stages) & 1), a.status, abort_flag);
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        if (ok) {
-            const uint8_t* stage = stages + (size_t)s * a.stage_bytes;
+    // ------------------------------------------------------------- MMA warps
+    // One mma.sync m16n8k16 covers 16 weight rows x 16 columns of a group x 8
+    // N slots = 4 input rows x {hi, lo} piece.  N tile nt holds input rows
+    // 4nt..4nt+3 of the chunk; the second N tile runs only for chunks of more
+    // than 4 picks.  For group column c = 8t + j (j = 0..7), mma 0 takes
+    // j in {0, 4 | 1, 5} and mma 1 takes j in {2, 6 | 3, 7} (K slots 2t, 2t+1 |
+    // 2t+8, 2t+9), which is the order unpack_q4 / unpack_q8 produce.
+    const int q0 = warp * QPW;  // this warp's first quad of K
+    const int nq = min(QPW, a.NQ - q0);
+    const int K = a.K;
+    uint32_t bf[QPW][2][4][4];  // [quad][N tile][group][mma 0 b0, b1, mma 1 b0, b1]
+    int ke = -1, kc = -1;
+    bool two = false;
+    int s = 0, r = 0;
+    uint32_t ph = 0, rph = 0;
+    for (int64_t it = 0; it < n_items; ++it, cur.next(pre, E, RTS)) {
+        if (cur.e != ke || cur.c != kc) {
+            ke = cur.e;
+            kc = cur.c;
+            const int pbase = (a.single_n ? 0 : a.offsets[ke]) + 8 * kc;
+            const int nvalid = min(8, (a.single_n ? a.single_n : a.counts[ke]) - 8 * kc);
+            two = nvalid > 4;
 #pragma unroll
-            for (int qi = 0; qi < kMaxQPW; ++qi) {
-                if (qi < nq) {
-                    const uint8_t* blk = stage + (size_t)(q0 + qi) * kBlock;
-                    uint32_t wg[8], wh[8];
-                    if (Q8) {
-                        const uint4 a0 = *reinterpret_cast<const uint4*>(blk + g * 64 + t * 16);
-                        const uint4 a1 = *reinterpret_cast<const uint4*>(blk + 1024 + g * 64 + t * 16);
-                        const uint4 b0 = *reinterpret_cast<const uint4*>(blk + (g + 8) * 64 + t * 16);
-                        const uint4 b1 = *reinterpret_cast<const uint4*>(blk + 1024 + (g + 8) * 64 + t * 16);
-                        wg[0] = a0.x; wg[1] = a0.y; wg[2] = a0.z; wg[3] = a0.w;
-                        wg[4] = a1.x; wg[5] = a1.y; wg[6] = a1.z; wg[7] = a1.w;
-                        wh[0] = b0.x; wh[1] = b0.y; wh[2] = b0.z; wh[3] = b0.w;
-                        wh[4] = b1.x; wh[5] = b1.y; wh[6] = b1.z; wh[7] = b1.w;
+            for (int nt = 0; nt < 2; ++nt) {
+                // this lane supplies N slot g: input row 4nt + (g >> 1), piece g & 1
+                const int xr = 4 * nt + (g >> 1);
+                const bool lo_piece = g & 1;
+                const bool valid = xr < nvalid;
+                const float* src = nullptr;
+                float up = 1.0f;
+                if (valid) {
+                    int ex;
+                    if (a.phase == 1) {
+                        const int row = a.sorted_rows[pbase + xr];
+                        src = a.x + (int64_t)row * a.src_ld;
+                        ex = a.row_exp[row];
                     } else {
-                        const uint4 a0 = *reinterpret_cast<const uint4*>(blk + g * 64 + t * 16);
-                        const uint4 b0 = *reinterpret_cast<const uint4*>(blk + (g + 8) * 64 + t * 16);
-                        wg[0] = a0.x; wg[1] = a0.y; wg[2] = a0.z; wg[3] = a0.w;
-                        wh[0] = b0.x; wh[1] = b0.y; wh[2] = b0.z; wh[3] = b0.w;
+                        src = a.act + (int64_t)(pbase + xr) * a.src_ld;
+                        ex = mb_row_exponent(__uint_as_float(a.act_max[pbase + xr]));
                     }
-                    float sg[4], sh[4];
-                    scales4<Q8, F16S>(blk, kData, g, sg);
-                    scales4<Q8, F16S>(blk, kData, g + 8, sh);
+                    up = pow2f(ex);
+                }
+#pragma unroll
+                for (int qi = 0; qi < QPW; ++qi) {
 #pragma unroll
                     for (int gi = 0; gi < 4; ++gi) {
-                        uint32_t pg[4], ph[4];
-                        if (Q8) {
-                            unpack_q8(wg[2 * gi], wg[2 * gi + 1], pg);
-                            unpack_q8(wh[2 * gi], wh[2 * gi + 1], ph);
+                        float v[8];
+                        const int col0 = ((q0 + qi) * 4 + gi) * 32 + 8 * t;
+                        if (valid && qi < nq && col0 + 8 <= K) {
+                            const float4 u0 = *reinterpret_cast<const float4*>(src + col0);
+                            const float4 u1 = *reinterpret_cast<const float4*>(src + col0 + 4);
+                            v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
+                            v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
                         } else {
-                            unpack_q4(wg[gi], pg);
-                            unpack_q4(wh[gi], ph);
-                        }
-                        float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            mb_mma_f16(d, pg[j], ph[j], pg[j], ph[j], bf[qi][gi][j][0], bf[qi][gi][j][1], d);
-                        acc[0] = fmaf(d[0], sg[gi], acc[0]);
-                        acc[1] = fmaf(d[1], sg[gi], acc[1]);
-                        acc[2] = fmaf(d[2], sh[gi], acc[2]);
-                        acc[3] = fmaf(d[3], sh[gi], acc[3]);
+                            for (int j = 0; j < 8; ++j) v[j] = (valid && qi < nq && col0 + j < K) ? src[col0 + j] : 0.0f;
+                        }
+                        __half pc[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const float xs = v[j] * up;
+                            const __half h = __float2half_rn(xs);
+                            pc[j] = lo_piece ? __float2half_rn(xs - __half2float(h)) : h;
+                        }
+                        bf[qi][nt][gi][0] = mb_pack_h2(pc[0], pc[4]);
+                        bf[qi][nt][gi][1] = mb_pack_h2(pc[1], pc[5]);
+                        bf[qi][nt][gi][2] = mb_pack_h2(pc[2], pc[6]);
+                        bf[qi][nt][gi][3] = mb_pack_h2(pc[3], pc[7]);
                     }
                 }
             }
         }
-        __syncwarp();
-        if (lane == 0) mb_mbar_arrive(&empty[s]);
 
-        float* rb = red + ((it & 1) * a.KW + warp) * 128;
-        *reinterpret_cast<float2*>(rb + g * 8 + 2 * t) = make_float2(acc[0], acc[1]);
-        *reinterpret_cast<float2*>(rb + (g + 8) * 8 + 2 * t) = make_float2(acc[2], acc[3]);
-        mb_named_barrier(1, nthr);
-
-        const float* rr = red + (it & 1) * a.KW * 128;
-        if (a.phase == 1) {
-            for (int o = tid; o < 64; o += nthr) {
-                const int jl = o >> 3, n = o & 7;
-                float gate = 0.f, upv = 0.f;
-                for (int w = 0; w < a.KW; ++w) {
-                    gate += rr[w * 128 + jl * 8 + n];
-                    upv += rr[w * 128 + (jl + 8) * 8 + n];
-                }
-                gate *= fs[0];
-                upv *= fs[0];
-                const float act = gate / (1.0f + expf(-gate)) * upv;
-                if (n < nvalid) {
-                    a.act[(int64_t)(pbase + n) * a.act_ld + 8 * rt + jl] = act;
-                    rmax = fmaxf(rmax, fabsf(act));
-                }
-            }
-        } else {
+        const int ntiles = min(MT, RT - cur.sg * MT);
+        if (it >= NR) mb_mbar_wait(&rempty[r], rph ^ 1u, a.status, abort_flag);
+        const bool ok = mb_mbar_wait(&full[s], ph, a.status, abort_flag);
+        float* rb = red + r * red_buf + warp * MT * kRedTile;
+        for (int mt = 0; mt < ntiles; ++mt) {
+            float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [N tile][row g, row g+8] of input row 4nt + t
+            if (ok) {
 #pragma unroll
-            for (int m = 0; m < 4; ++m) {
-                const int o = tid + m * nthr;
-                if (o < 128) {
-                    const int row = o & 15, n = o >> 4;
-                    float v = 0.f;
-                    for (int w = 0; w < a.KW; ++w) v += rr[w * 128 + row * 8 + n];
-                    const int orow = 16 * rt + row;
-                    if (n < nvalid && orow < a.O_real) a.y[(int64_t)(pbase + n) * a.y_ld + orow] = v * fs[m];
+                for (int qi = 0; qi < QPW; ++qi) {
+                    if (qi < nq) {
+                        const uint8_t* blk =
+                            stages + (size_t)s * stage_bytes + (size_t)mt * tile_bytes + (size_t)(q0 + qi) * kBlock;
+                        uint32_t wg[Q8 ? 8 : 4], wh[Q8 ? 8 : 4];
+                        {
+                            const uint4 a0 = *reinterpret_cast<const uint4*>(blk + g * 64 + t * 16);
+                            const uint4 b0 = *reinterpret_cast<const uint4*>(blk + (g + 8) * 64 + t * 16);
+                            wg[0] = a0.x; wg[1] = a0.y; wg[2] = a0.z; wg[3] = a0.w;
+                            wh[0] = b0.x; wh[1] = b0.y; wh[2] = b0.z; wh[3] = b0.w;
+                        }
+                        if (Q8) {
+                            const uint4 a1 = *reinterpret_cast<const uint4*>(blk + 1024 + g * 64 + t * 16);
+                            const uint4 b1 = *reinterpret_cast<const uint4*>(blk + 1024 + (g + 8) * 64 + t * 16);
+                            wg[Q8 ? 4 : 0] = a1.x; wg[Q8 ? 5 : 1] = a1.y; wg[Q8 ? 6 : 2] = a1.z; wg[Q8 ? 7 : 3] = a1.w;
+                            wh[Q8 ? 4 : 0] = b1.x; wh[Q8 ? 5 : 1] = b1.y; wh[Q8 ? 6 : 2] = b1.z; wh[Q8 ? 7 : 3] = b1.w;
+                        }
+                        float sg[4], sh[4];
+                        scales4<F16S>(blk + kData + g * (F16S ? 8 : 16), sg);
+                        scales4<F16S>(blk + kData + (g + 8) * (F16S ? 8 : 16), sh);
+#pragma unroll
+                        for (int gi = 0; gi < 4; ++gi) {
+                            uint32_t pg[4], ph_[4];
+                            if (Q8) {
+                                unpack_q8(wg[(2 * gi) % (Q8 ? 8 : 4)], wg[(2 * gi + 1) % (Q8 ? 8 : 4)], pg);
+                                unpack_q8(wh[(2 * gi) % (Q8 ? 8 : 4)], wh[(2 * gi + 1) % (Q8 ? 8 : 4)], ph_);
+                            } else {
+                                unpack_q4(wg[gi], pg);
+                                unpack_q4(wh[gi], ph_);
+                            }
+                            float d[4];
+                            mb_mma_f16_zero(d, pg[0], ph_[0], pg[1], ph_[1], bf[qi][0][gi][0], bf[qi][0][gi][1]);
+                            mb_mma_f16(d, pg[2], ph_[2], pg[3], ph_[3], bf[qi][0][gi][2], bf[qi][0][gi][3]);
+                            acc[0][0] = fmaf(d[0] + d[1], sg[gi], acc[0][0]);
+                            acc[0][1] = fmaf(d[2] + d[3], sh[gi], acc[0][1]);
+                            if (two) {
+                                float e[4];
+                                mb_mma_f16_zero(e, pg[0], ph_[0], pg[1], ph_[1], bf[qi][1][gi][0], bf[qi][1][gi][1]);
+                                mb_mma_f16(e, pg[2], ph_[2], pg[3], ph_[3], bf[qi][1][gi][2], bf[qi][1][gi][3]);
+                                acc[1][0] = fmaf(e[0] + e[1], sg[gi], acc[1][0]);
+                                acc[1][1] = fmaf(e[2] + e[3], sh[gi], acc[1][1]);
+                            }
+                        }
+                    }
                 }
             }
+            float* rt = rb + mt * kRedTile;  // [input row n][16 rows]
+            rt[t * 16 + g] = acc[0][0];
+            rt[t * 16 + g + 8] = acc[0][1];
+            rt[(4 + t) * 16 + g] = acc[1][0];
+            rt[(4 + t) * 16 + g + 8] = acc[1][1];
+        }
+        __syncwarp();
+        if (lane == 0) {
+            mb_mbar_arrive(&empty[s]);
+            mb_mbar_arrive(&rfull[r]);
+        }
+        if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+        }
+        if (++r == NR) {
+            r = 0;
+            rph ^= 1u;
         }
     }
-    flush_max();
 }
 
 struct Cfg {
-    int QPW, KW, NQ, stages, stage_bytes;
+    int KW, NQ, QPW, MT, stages, tile_bytes, nred;
     size_t smem;
 };
 
-Cfg plan(int fmt, int K, int E, int max_stage_smem)
+#ifndef MB_DECODE_QPW_MIN_NQ
+#define MB_DECODE_QPW_MIN_NQ 99  // two quads per MMA warp from this many quads of K (measured slower: off)
+#endif
+
+// Stage = MT row tiles of ~32 KB; as many stages as fit in the shared memory
+// of one CTA per SM (many MMA warps) or of two (few MMA warps: short K).
+Cfg plan(int fmt, int K, int E, int RT)
 {
     Cfg c;
     const Fmt f = fmt_info(fmt);
     c.NQ = (K + 127) / 128;
-    c.QPW = c.NQ >= 2 ? 2 : 1;
+    c.QPW = c.NQ >= MB_DECODE_QPW_MIN_NQ ? 2 : 1;
     c.KW = (c.NQ + c.QPW - 1) / c.QPW;
-    c.stage_bytes = c.NQ * f.block_bytes;
-    c.stages = max_stage_smem / c.stage_bytes;
-    if (c.stages > 8) c.stages = 8;
-    if (c.stages < 2) c.stages = 2;
-    c.smem = (size_t)c.stages * c.stage_bytes + 2 * c.KW * 128 * sizeof(float) + 2 * c.stages * sizeof(uint64_t) +
-             (E + 1) * sizeof(int64_t) + 16;
+    c.tile_bytes = c.NQ * f.block_bytes;
+    c.MT = (32 * 1024 + c.tile_bytes / 2) / c.tile_bytes;
+    c.MT = c.MT < 1 ? 1 : (c.MT > kMaxMT ? kMaxMT : c.MT);
+    if (c.MT > RT) c.MT = RT < 1 ? 1 : RT;
+    c.nred = kEpiWarps;
+    const size_t budget = c.KW <= 8 ? 110 * 1024 : 210 * 1024;
+    const size_t red = (size_t)c.nred * c.KW * c.MT * kRedTile * sizeof(float);
+    const size_t fixed = red + (size_t)(E + 1) * sizeof(int64_t) + 64 + 16 * sizeof(uint64_t);
+    const size_t stage = (size_t)c.MT * c.tile_bytes;
+    int st = budget > fixed ? (int)((budget - fixed) / stage) : 2;
+    c.stages = st < 2 ? 2 : (st > 8 ? 8 : st);
+    c.smem = (size_t)c.stages * stage + red + (size_t)(2 * c.stages + 2 * c.nred) * sizeof(uint64_t) +
+             (size_t)(E + 1) * sizeof(int64_t) + 16;
     return c;
 }
 
@@ -410,23 +532,50 @@ template <int FMT>
 int launch_phase(const DecodeArgs& base, int K, int RT, cudaStream_t st)
 {
     DecodeArgs a = base;
-    const Cfg c = plan(FMT, K, a.E, 96 * 1024);
-    if (c.KW > kMaxKW)
-        return mb_fail(MB_EUNSUPPORTED, "mb_moe_decode: K=%d needs %d consumer warps (max %d)", K, c.KW, kMaxKW);
+    const Cfg c = plan(FMT, K, a.E, RT);
+    if (c.KW * 32 + (1 + kEpiWarps) * 32 > threads_max(c.QPW))
+        return mb_fail(MB_EUNSUPPORTED, "mb_moe_decode: K=%d needs %d MMA warps (max %d)", K, c.KW,
+                       threads_max(c.QPW) / 32 - 1 - kEpiWarps);
     a.K = K;
     a.NQ = c.NQ;
     a.RT = RT;
-    a.QPW = c.QPW;
+    a.MT = c.MT;
     a.KW = c.KW;
     a.stages = c.stages;
-    a.stage_bytes = c.stage_bytes;
-    auto kern = moe_decode_kernel<FMT>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem);
-    if (e != cudaSuccess) return mb_fail(MB_ECUDA, "mb_moe_decode: smem attribute: %s", cudaGetErrorString(e));
-    const int threads = (c.KW + 1) * 32;
-    int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, c.smem);
-    if (e != cudaSuccess || per_sm < 1) per_sm = 1;
+    a.tile_bytes = c.tile_bytes;
+    a.nred = c.nred;
+    auto kern = c.QPW == 2 ? moe_decode_kernel<FMT, 2> : moe_decode_kernel<FMT, 1>;
+    const int threads = (c.KW + 1 + kEpiWarps) * 32;
+    // one-time per (device, kernel, configuration): raise the shared-memory
+    // limit and look up the occupancy, so later calls (and graph captures) only
+    // enqueue work
+    struct Occ {
+        int dev, threads;
+        size_t smem;
+        int per_sm, qpw;
+    };
+    static thread_local Occ cache[16];
+    static thread_local int ncache = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int per_sm = -1;
+    for (int i = 0; i < ncache; ++i)
+        if (cache[i].dev == dev && cache[i].threads == threads && cache[i].smem == c.smem && cache[i].qpw == c.QPW)
+            per_sm = cache[i].per_sm;
+    // the shared-memory limit is an attribute of the kernel, shared by every
+    // configuration that launches it: only ever raise it
+    static thread_local size_t smem_attr[2][64] = {{0}};
+    const int di = dev & 63, ki = c.QPW - 1;
+    if (smem_attr[ki][di] < c.smem) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem);
+        if (e != cudaSuccess) return mb_fail(MB_ECUDA, "mb_moe_decode: smem attribute: %s", cudaGetErrorString(e));
+        smem_attr[ki][di] = c.smem;
+    }
+    if (per_sm < 0) {
+        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, c.smem);
+        if (e != cudaSuccess || per_sm < 1) per_sm = 1;
+        if (ncache < 16) cache[ncache++] = Occ{dev, threads, c.smem, per_sm, c.QPW};
+    }
     const int grid = mb_num_sms() * per_sm;
     kern<<<grid, threads, c.smem, st>>>(a);
     return mb_check_launch("mb_moe_decode");

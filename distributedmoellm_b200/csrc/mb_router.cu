@@ -7,57 +7,55 @@
 
 namespace {
 
-constexpr int kLogitTokens = 8;   // tokens per CTA of the logits kernel
-constexpr int kLogitExperts = 8;  // experts per CTA (one per warp)
+// Router logits as a split-K f32 product: CTA (token block, expert block,
+// K slice) writes partial dot products of its 256 columns; the top-k kernel
+// adds the slices in slice order (deterministic) before the softmax.
+constexpr int kLgT = 16;    // tokens per CTA
+constexpr int kLgE = 16;    // experts per CTA
+constexpr int kLgK = 256;   // columns per K slice
 
-// logits[t][e] = sum_h x[t][h] * router[e][h].  CTAs with blockIdx.x == 0
-// also write each token's row exponent (its largest |x|) when asked.
-__global__ void __launch_bounds__(256) router_logits_kernel(const float* __restrict__ x,
-                                                            const float* __restrict__ router, int64_t T, int H, int E,
-                                                            float* __restrict__ logits, int32_t* __restrict__ row_exp)
+__global__ void __launch_bounds__(256) router_partial_kernel(const float* __restrict__ x,
+                                                             const float* __restrict__ router, int64_t T, int H,
+                                                             int E, float* __restrict__ part,
+                                                             float* __restrict__ part_max)
 {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int e = blockIdx.x * kLogitExperts + warp;
-    const int64_t t0 = (int64_t)blockIdx.y * kLogitTokens;
-    const int nt = (int)((T - t0) < kLogitTokens ? (T - t0) : kLogitTokens);
-    const bool vec = (H & 3) == 0;
-    if (e < E) {
-        float acc[kLogitTokens];
-#pragma unroll
-        for (int i = 0; i < kLogitTokens; ++i) acc[i] = 0.0f;
-        const float* w = router + (int64_t)e * H;
-        if (vec) {
-            for (int h = lane * 4; h < H; h += 128) {
-                const float4 wv = *reinterpret_cast<const float4*>(w + h);
-#pragma unroll
-                for (int i = 0; i < kLogitTokens; ++i) {
-                    if (i < nt) {
-                        const float4 xv = *reinterpret_cast<const float4*>(x + (t0 + i) * H + h);
-                        acc[i] = fmaf(wv.x, xv.x, fmaf(wv.y, xv.y, fmaf(wv.z, xv.z, fmaf(wv.w, xv.w, acc[i]))));
-                    }
-                }
-            }
-        } else {
-            for (int h = lane; h < H; h += 32) {
-                const float wv = w[h];
-#pragma unroll
-                for (int i = 0; i < kLogitTokens; ++i)
-                    if (i < nt) acc[i] = fmaf(wv, x[(t0 + i) * H + h], acc[i]);
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < kLogitTokens; ++i) {
-            float v = acc[i];
-            for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0 && i < nt) logits[(t0 + i) * E + e] = v;
-        }
+    __shared__ float xs[kLgT][kLgK + 4];
+    __shared__ float ws[kLgE][kLgK + 4];
+    const int64_t t0 = (int64_t)blockIdx.x * kLgT;
+    const int e0 = blockIdx.y * kLgE, ks = blockIdx.z, k0 = ks * kLgK;
+    const int kn = min(kLgK, H - k0);
+    for (int i = threadIdx.x; i < kLgT * (kLgK / 4); i += 256) {
+        const int r = i / (kLgK / 4), c = (i % (kLgK / 4)) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t0 + r < T && c < kn) v = *reinterpret_cast<const float4*>(x + (t0 + r) * H + k0 + c);
+        *reinterpret_cast<float4*>(&xs[r][c]) = v;
     }
-    if (row_exp && blockIdx.x == 0 && warp < nt) {
-        const float* xr = x + (t0 + warp) * H;
-        float m = 0.0f;
-        for (int h = lane; h < H; h += 32) m = fmaxf(m, fabsf(xr[h]));
-        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (lane == 0) row_exp[t0 + warp] = mb_row_exponent(m);
+    for (int i = threadIdx.x; i < kLgE * (kLgK / 4); i += 256) {
+        const int r = i / (kLgK / 4), c = (i % (kLgK / 4)) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (e0 + r < E && c < kn) v = *reinterpret_cast<const float4*>(router + (int64_t)(e0 + r) * H + k0 + c);
+        *reinterpret_cast<float4*>(&ws[r][c]) = v;
+    }
+    __syncthreads();
+    // thread -> (token ti, expert ej): 16 x 16 threads
+    const int ti = threadIdx.x >> 4, ej = threadIdx.x & 15;
+    float a0 = 0.f;
+#pragma unroll 8
+    for (int c = 0; c < kLgK; c += 4) {
+        const float4 xv = *reinterpret_cast<const float4*>(&xs[ti][c]);
+        const float4 w0 = *reinterpret_cast<const float4*>(&ws[ej][c]);
+        a0 = fmaf(xv.x, w0.x, fmaf(xv.y, w0.y, fmaf(xv.z, w0.z, fmaf(xv.w, w0.w, a0))));
+    }
+    const int64_t t = t0 + ti;
+    if (t < T && e0 + ej < E) part[((int64_t)ks * T + t) * E + e0 + ej] = a0;
+    if (part_max && blockIdx.y == 0) {  // this slice's largest |x| of each token
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        for (int r = warp; r < kLgT; r += 8) {
+            float m = 0.f;
+            for (int c = lane; c < kLgK; c += 32) m = fmaxf(m, fabsf(xs[r][c]));
+            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if (lane == 0 && t0 + r < T) part_max[(int64_t)ks * T + t0 + r] = m;
+        }
     }
 }
 
@@ -80,21 +78,39 @@ __global__ void row_exponent_kernel(const float* __restrict__ x, int64_t T, int 
 // picks, renormalised over the k picks when asked (model.py:164-166).
 constexpr int kTopkMaxPerLane = 32;  // E <= 1024
 
-__global__ void router_topk_kernel(const float* __restrict__ logits, int64_t T, int E, int k, int normalize,
-                                   int32_t* __restrict__ idx, float* __restrict__ w)
+// With nslices > 0 the logits are first summed from nslices partial slices
+// (slice s at logits + s*T*E) in slice order, written to out_logits when
+// given, and row_exp gets each token's exponent from the slices' maxima.
+__global__ void router_topk_kernel(const float* __restrict__ logits, int nslices, const float* __restrict__ part_max,
+                                   float* __restrict__ out_logits, int32_t* __restrict__ row_exp, int64_t T, int E,
+                                   int k, int normalize, int32_t* __restrict__ idx, float* __restrict__ w)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
     if (t >= T) return;
-    const float* lg = logits + t * E;
     const int per = (E + 31) / 32;
     float v[kTopkMaxPerLane];
     float m = -FLT_MAX;
 #pragma unroll
     for (int i = 0; i < kTopkMaxPerLane; ++i) {
         const int e = i * 32 + lane;
-        v[i] = (i < per && e < E) ? lg[e] : -INFINITY;
-        if (i < per && e < E) m = fmaxf(m, v[i]);
+        float val = -INFINITY;
+        if (i < per && e < E) {
+            if (nslices > 0) {
+                val = 0.f;
+                for (int sl = 0; sl < nslices; ++sl) val += logits[((int64_t)sl * T + t) * E + e];
+                if (out_logits) out_logits[t * E + e] = val;
+            } else {
+                val = logits[t * E + e];
+            }
+            m = fmaxf(m, val);
+        }
+        v[i] = val;
+    }
+    if (row_exp && part_max && lane == 0) {
+        float xm = 0.f;
+        for (int sl = 0; sl < nslices; ++sl) xm = fmaxf(xm, part_max[(int64_t)sl * T + t]);
+        row_exp[t] = mb_row_exponent(xm);
     }
     for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float sum = 0.0f;
@@ -105,9 +121,8 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int64_t T, 
     }
     for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     uint32_t taken = 0;  // bit i: element i of this lane already picked
-    float pk[32];
-    int ik[32];
-    float psum = 0.0f;
+    float my_p = 0.f, psum = 0.f;
+    int my_i = -1;
     for (int j = 0; j < k; ++j) {
         float bv = -INFINITY;
         int bi = INT32_MAX;
@@ -129,17 +144,15 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int64_t T, 
         }
         if (bi != INT32_MAX && (bi & 31) == lane) taken |= 1u << (bi >> 5);
         const float p = (bi == INT32_MAX) ? 0.0f : expf(bv - m) / sum;
-        if (j < 32) {
-            pk[j] = p;
-            ik[j] = bi;
+        if (lane == j) {
+            my_p = p;
+            my_i = bi;
         }
         psum += p;
     }
-    if (lane == 0) {
-        for (int j = 0; j < k && j < 32; ++j) {
-            idx[t * k + j] = ik[j];
-            w[t * k + j] = normalize ? pk[j] / psum : pk[j];
-        }
+    if (lane < k) {
+        idx[t * k + lane] = my_i;
+        w[t * k + lane] = normalize ? my_p / psum : my_p;
     }
 }
 
@@ -183,24 +196,53 @@ __global__ void __launch_bounds__(kPermWarps * 32) permute_kernel(
         tot[e] = run;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {  // exclusive scan over experts (E <= 1024: serial is fine)
-        int32_t run = 0, u = 0;
-        for (int e = 0; e < E; ++e) {
-            const int32_t c = tot[e];
-            offsets[e] = run;
+    {  // exclusive scan of the totals over experts, and the compact list of used experts
+        __shared__ int32_t wsum[kPermWarps], wcnt[kPermWarps];
+        const int e = threadIdx.x;                    // blockDim.x = 1024 >= E
+        const int32_t c = e < E ? tot[e] : 0;
+        int32_t inc = c, used = (c > 0);
+        for (int o = 1; o < 32; o <<= 1) {
+            const int32_t u = __shfl_up_sync(0xffffffffu, inc, o), v = __shfl_up_sync(0xffffffffu, used, o);
+            if (lane >= o) {
+                inc += u;
+                used += v;
+            }
+        }
+        if (lane == 31) {
+            wsum[warp] = inc;
+            wcnt[warp] = used;
+        }
+        __syncthreads();
+        if (warp == 0) {
+            int32_t s1 = wsum[lane], s2 = wcnt[lane];
+            for (int o = 1; o < 32; o <<= 1) {
+                const int32_t u = __shfl_up_sync(0xffffffffu, s1, o), v = __shfl_up_sync(0xffffffffu, s2, o);
+                if (lane >= o) {
+                    s1 += u;
+                    s2 += v;
+                }
+            }
+            wsum[lane] = s1;
+            wcnt[lane] = s2;
+        }
+        __syncthreads();
+        const int32_t excl = inc - c + (warp ? wsum[warp - 1] : 0);
+        const int32_t uidx = used - (c > 0) + (warp ? wcnt[warp - 1] : 0);
+        __syncthreads();
+        if (e < E) {
+            offsets[e] = excl;
             if (counts) counts[e] = c;
             if (c > 0) {
-                if (uexperts) uexperts[u] = e;
-                if (uoffsets) uoffsets[u] = run;
-                ++u;
+                if (uexperts) uexperts[uidx] = e;
+                if (uoffsets) uoffsets[uidx] = excl;
             }
-            tot[e] = run;
-            run += c;
+            tot[e] = excl;
         }
-        offsets[E] = run;
-        if (uoffsets) uoffsets[u] = run;
-        if (n_unique) *n_unique = u;
-        tot[E] = run;
+        if (e == E - 1) {
+            offsets[E] = excl + c;
+            if (uoffsets) uoffsets[uidx + (c > 0)] = excl + c;
+            if (n_unique) *n_unique = uidx + (c > 0);
+        }
     }
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
@@ -232,7 +274,8 @@ __global__ void __launch_bounds__(kPermWarps * 32) permute_kernel(
     }
 }
 
-// out[r] (+)= sum_i pair_w[i] * y[pair_idx[i]]; one CTA row-slice per (row, 1024 columns).
+// out[r] (+)= sum_i pair_w[i] * y[pair_idx[i]] in entry order; one thread per
+// 4 columns of a row.  Rows with up to 8 entries issue all their loads first.
 __global__ void combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ row_ptr,
                                const int32_t* __restrict__ pair_idx, const float* __restrict__ pair_w, int64_t T,
                                int k, int H, int accumulate, float* __restrict__ out)
@@ -243,31 +286,99 @@ __global__ void combine_kernel(const float* __restrict__ y, const int32_t* __res
     const int64_t i0 = row_ptr ? row_ptr[r] : r * k;
     const int64_t i1 = row_ptr ? row_ptr[r + 1] : r * k + k;
     float4 acc = accumulate ? *reinterpret_cast<const float4*>(out + r * H + h) : make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int64_t i = i0; i < i1; ++i) {
-        const int32_t p = pair_idx[i];
-        if (p < 0) continue;
-        const float wt = pair_w[i];
-        const float4 v = *reinterpret_cast<const float4*>(y + (int64_t)p * H + h);
-        acc.x = fmaf(wt, v.x, acc.x);
-        acc.y = fmaf(wt, v.y, acc.y);
-        acc.z = fmaf(wt, v.z, acc.z);
-        acc.w = fmaf(wt, v.w, acc.w);
+    for (int64_t b = i0; b < i1; b += 8) {
+        int32_t p[8];
+        float wt[8];
+        float4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            p[j] = (b + j < i1) ? pair_idx[b + j] : -1;
+            wt[j] = (b + j < i1) ? pair_w[b + j] : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            v[j] = p[j] >= 0 ? *reinterpret_cast<const float4*>(y + (int64_t)p[j] * H + h) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (p[j] < 0) continue;
+            acc.x = fmaf(wt[j], v[j].x, acc.x);
+            acc.y = fmaf(wt[j], v[j].y, acc.y);
+            acc.z = fmaf(wt[j], v[j].z, acc.z);
+            acc.w = fmaf(wt[j], v[j].w, acc.w);
+        }
     }
     *reinterpret_cast<float4*>(out + r * H + h) = acc;
 }
 
 }  // namespace
 
-extern "C" int mb_router_logits(const float* x, const float* router, int64_t T, int H, int E, float* logits,
-                                int32_t* row_exp, void* stream)
+static int router_slices(int H) { return (H + kLgK - 1) / kLgK; }
+
+__global__ void sum_slices_kernel(const float* __restrict__ part, int nslices, const float* __restrict__ part_max,
+                                  int64_t T, int E, float* __restrict__ logits, int32_t* __restrict__ row_exp)
 {
-    MB_REQUIRE(x && router && logits, "mb_router_logits: null pointer");
-    MB_REQUIRE(T >= 0 && H > 0 && E > 0, "mb_router_logits: bad shape");
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < T * E) {
+        float v = 0.f;
+        for (int sl = 0; sl < nslices; ++sl) v += part[(int64_t)sl * T * E + i];
+        logits[i] = v;
+    }
+    if (row_exp && i < T) {
+        float m = 0.f;
+        for (int sl = 0; sl < nslices; ++sl) m = fmaxf(m, part_max[(int64_t)sl * T + i]);
+        row_exp[i] = mb_row_exponent(m);
+    }
+}
+
+static int launch_partial(const float* x, const float* router, int64_t T, int H, int E, float* part,
+                          float* part_max, cudaStream_t st)
+{
+    MB_REQUIRE(x && router && part, "router logits: null pointer");
+    MB_REQUIRE(T >= 0 && H > 0 && E > 0 && H % 4 == 0, "router logits: bad shape (H must be a multiple of 4)");
+    MB_REQUIRE(((uintptr_t)x & 15) == 0 && ((uintptr_t)router & 15) == 0, "router logits: x/router not 16-byte aligned");
+    MB_REQUIRE((T + kLgT - 1) / kLgT <= 0x7fffffff && (E + kLgE - 1) / kLgE <= 65535, "router logits: too large");
     if (T == 0) return MB_OK;
-    MB_REQUIRE(T / kLogitTokens < 65535, "mb_router_logits: T too large");
-    dim3 grid((E + kLogitExperts - 1) / kLogitExperts, (unsigned)((T + kLogitTokens - 1) / kLogitTokens));
-    router_logits_kernel<<<grid, 256, 0, mb_stream(stream)>>>(x, router, T, H, E, logits, row_exp);
+    dim3 grid((unsigned)((T + kLgT - 1) / kLgT), (E + kLgE - 1) / kLgE, router_slices(H));
+    router_partial_kernel<<<grid, 256, 0, st>>>(x, router, T, H, E, part, part_max);
+    return mb_check_launch("router logits");
+}
+
+extern "C" int64_t mb_router_workspace_bytes(int64_t T, int H, int E)
+{
+    const int64_t ns = router_slices(H);
+    return ((ns * T * E * 4 + 255) / 256) * 256 + ((ns * T * 4 + 255) / 256) * 256;
+}
+
+extern "C" int mb_router_logits(const float* x, const float* router, int64_t T, int H, int E, float* logits,
+                                int32_t* row_exp, void* workspace, int64_t workspace_bytes, void* stream)
+{
+    MB_REQUIRE(logits && workspace, "mb_router_logits: null pointer");
+    MB_REQUIRE(workspace_bytes >= mb_router_workspace_bytes(T, H, E), "mb_router_logits: workspace too small");
+    const int ns = router_slices(H);
+    float* part = reinterpret_cast<float*>(workspace);
+    float* pmax = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + (((int64_t)ns * T * E * 4 + 255) / 256) * 256);
+    int rc = launch_partial(x, router, T, H, E, part, pmax, mb_stream(stream));
+    if (rc || T == 0) return rc;
+    sum_slices_kernel<<<(unsigned)((T * E + 255) / 256), 256, 0, mb_stream(stream)>>>(part, ns, pmax, T, E, logits,
+                                                                                     row_exp);
     return mb_check_launch("mb_router_logits");
+}
+
+extern "C" int mb_router_route(const float* x, const float* router, int64_t T, int H, int E, int k, int normalize,
+                               float* logits, int32_t* row_exp, int32_t* idx, float* w, void* workspace,
+                               int64_t workspace_bytes, void* stream)
+{
+    MB_REQUIRE(idx && w && workspace, "mb_router_route: null pointer");
+    MB_REQUIRE(E <= 32 * kTopkMaxPerLane && k > 0 && k <= E && k <= 32, "mb_router_route: E=%d k=%d", E, k);
+    MB_REQUIRE(workspace_bytes >= mb_router_workspace_bytes(T, H, E), "mb_router_route: workspace too small");
+    const int ns = router_slices(H);
+    float* part = reinterpret_cast<float*>(workspace);
+    float* pmax = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + (((int64_t)ns * T * E * 4 + 255) / 256) * 256);
+    int rc = launch_partial(x, router, T, H, E, part, pmax, mb_stream(stream));
+    if (rc || T == 0) return rc;
+    router_topk_kernel<<<(unsigned)((T + 7) / 8), 256, 0, mb_stream(stream)>>>(part, ns, pmax, logits, row_exp, T, E,
+                                                                               k, normalize, idx, w);
+    return mb_check_launch("mb_router_route");
 }
 
 extern "C" int mb_row_exponents(const float* x, int64_t T, int H, int32_t* row_exp, void* stream)
@@ -285,7 +396,8 @@ extern "C" int mb_router_topk(const float* logits, int64_t T, int E, int k, int 
     MB_REQUIRE(E > 0 && E <= 32 * kTopkMaxPerLane, "mb_router_topk: E=%d outside 1..1024", E);
     MB_REQUIRE(k > 0 && k <= E && k <= 32, "mb_router_topk: k=%d outside 1..min(E,32)", k);
     if (T == 0) return MB_OK;
-    router_topk_kernel<<<(unsigned)((T + 7) / 8), 256, 0, mb_stream(stream)>>>(logits, T, E, k, normalize, idx, w);
+    router_topk_kernel<<<(unsigned)((T + 7) / 8), 256, 0, mb_stream(stream)>>>(logits, 0, nullptr, nullptr, nullptr,
+                                                                               T, E, k, normalize, idx, w);
     return mb_check_launch("mb_router_topk");
 }
 
@@ -314,7 +426,7 @@ extern "C" int mb_unpermute_combine(const float* y, const int32_t* row_ptr, cons
     MB_REQUIRE(y && pair_idx && pair_w && out, "mb_unpermute_combine: null pointer");
     MB_REQUIRE(H % 4 == 0 && ((uintptr_t)y & 15) == 0 && ((uintptr_t)out & 15) == 0,
                "mb_unpermute_combine: H must be a multiple of 4 and y/out 16-byte aligned");
-    MB_REQUIRE(T < 65536 * 1024LL, "mb_unpermute_combine: T too large");
+    MB_REQUIRE(T <= 65535, "mb_unpermute_combine: T=%lld above 65535", (long long)T);
     if (T == 0) return MB_OK;
     dim3 grid((H / 4 + 255) / 256, (unsigned)T);
     combine_kernel<<<grid, 256, 0, mb_stream(stream)>>>(y, row_ptr, pair_idx, pair_w, T, k, H, accumulate, out);

@@ -70,14 +70,40 @@ def gguf_dequant(raw: torch.Tensor, qtype: int, cols: int, out: torch.Tensor | N
 
 # ---- router -------------------------------------------------------------------------
 
-def router_logits(x: torch.Tensor, router: torch.Tensor, logits=None, row_exp=None):
+def router_workspace_bytes(T: int, H: int, E: int) -> int:
+    return int(lib().mb_router_workspace_bytes(T, H, E))
+
+
+def _router_ws(T, H, E, ws, device):
+    need = router_workspace_bytes(T, H, E)
+    if ws is None:
+        ws = torch.empty(need, dtype=torch.uint8, device=device)
+    return ws
+
+
+def router_logits(x: torch.Tensor, router: torch.Tensor, logits=None, row_exp=None, workspace=None):
     _cuda(x, router)
     T, H = x.shape
     E = router.shape[0]
     logits = torch.empty((T, E), dtype=torch.float32, device=x.device) if logits is None else logits
-    check(lib().mb_router_logits(_p(x), _p(router), T, H, E, _p(logits), _p(row_exp), _stream()),
-          "mb_router_logits")
+    ws = _router_ws(T, H, E, workspace, x.device)
+    check(lib().mb_router_logits(_p(x), _p(router), T, H, E, _p(logits), _p(row_exp), _p(ws), ws.numel(),
+                                 _stream()), "mb_router_logits")
     return logits
+
+
+def router_route(x: torch.Tensor, router: torch.Tensor, k: int, normalize: bool, idx=None, w=None, logits=None,
+                 row_exp=None, workspace=None):
+    """Logits + top-k in two launches; returns (idx, w)."""
+    _cuda(x, router)
+    T, H = x.shape
+    E = router.shape[0]
+    idx = torch.empty((T, k), dtype=torch.int32, device=x.device) if idx is None else idx
+    w = torch.empty((T, k), dtype=torch.float32, device=x.device) if w is None else w
+    ws = _router_ws(T, H, E, workspace, x.device)
+    check(lib().mb_router_route(_p(x), _p(router), T, H, E, k, int(bool(normalize)), _p(logits), _p(row_exp),
+                                _p(idx), _p(w), _p(ws), ws.numel(), _stream()), "mb_router_route")
+    return idx, w
 
 
 def row_exponents(x: torch.Tensor, out=None):

@@ -27,6 +27,7 @@ class _Buffers:
         self.routing = D.Routing(T, k, E, dev)
         self.y = torch.empty((max(P, 1), H), dtype=torch.float32, device=dev)
         self.ws = torch.empty(D.decode_workspace_bytes(P, I), dtype=torch.uint8, device=dev)
+        self.rws = torch.empty(D.router_workspace_bytes(T, H, E), dtype=torch.uint8, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.out = torch.empty((T, H), dtype=torch.float32, device=dev)
 
@@ -49,8 +50,7 @@ class MoELayer:
 
     def route(self, x: torch.Tensor) -> _Buffers:
         b = self.buffers(x.shape[0])
-        D.router_logits(x, self.router, b.logits, b.row_exp)
-        D.router_topk(b.logits, self.k, self.normalize, b.idx, b.w)
+        D.router_route(x, self.router, self.k, self.normalize, b.idx, b.w, b.logits, b.row_exp, b.rws)
         D.permute(b.idx, b.w, self.E, b.routing)
         return b
 
@@ -68,6 +68,24 @@ class MoELayer:
         return D.combine(b.y, b.routing.inv, b.w.view(-1), T, self.k, out=b.out if out is None else out)
 
     __call__ = forward
+
+    def capture(self, x: torch.Tensor, experts_only: bool = False) -> torch.cuda.CUDAGraph:
+        """A CUDA graph of forward(x) (or of the expert kernels alone, on the
+        routing of the last forward of this x) on x's current contents; replay
+        it after writing new inputs into x.  Output: buffers(T).out."""
+        b = self.buffers(x.shape[0])
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):          # warm-up outside capture (one-time set-up calls)
+            self.forward(x)
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            if experts_only:
+                self.experts_forward(x, b)
+            else:
+                self.forward(x)
+        return g
 
     def status(self, T: int) -> int:
         """The kernels' status word for token count T (0 = no failure)."""

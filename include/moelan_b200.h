@@ -66,10 +66,20 @@ int mb_gguf_dequant(const uint8_t *raw, int qtype, int64_t rows, int64_t row_byt
 
 /* ---- router ------------------------------------------------------------------ */
 
-/* Router logits h @ router.T (moelan/model.py:597) in f32, plus, when
- * row_exp != NULL, each row's power-of-two exponent used by the mat-vecs. */
+/* Workspace bytes of mb_router_logits / mb_router_route. */
+int64_t mb_router_workspace_bytes(int64_t T, int H, int E);
+
+/* Router logits h @ router.T (moelan/model.py:597) in f32 (split over 256-
+ * column slices, summed in slice order), plus, when row_exp != NULL, each
+ * row's power-of-two exponent used by the mat-vecs. */
 int mb_router_logits(const float *x, const float *router, int64_t T, int H, int E, float *logits,
-                     int32_t *row_exp, void *stream);
+                     int32_t *row_exp, void *workspace, int64_t workspace_bytes, void *stream);
+
+/* Logits and route in two launches: moelan/model.py:597 then model.py:160
+ * route(logits, top_k, normalize).  logits and row_exp may be NULL. */
+int mb_router_route(const float *x, const float *router, int64_t T, int H, int E, int k, int normalize,
+                    float *logits, int32_t *row_exp, int32_t *idx, float *w, void *workspace,
+                    int64_t workspace_bytes, void *stream);
 
 /* moelan/model.py:160 route(logits, top_k, normalize) with _top_k
  * (model.py:154-157): f32 softmax, k best experts (ties: lower id first),

@@ -100,6 +100,28 @@ def test_router_topk_matches_reference(D, golden, case):
     np.testing.assert_allclose(w[rows], golden[f"{name}_w"][rows], rtol=2e-6, atol=1e-7)
 
 
+@pytest.mark.parametrize("T,H,E,k", [(1, 2048, 128, 8), (37, 2048, 128, 8), (64, 256, 16, 2), (300, 4096, 8, 2),
+                                     (5, 200, 60, 6)])
+def test_router_logits_and_route(D, T, H, E, k):
+    rng = np.random.default_rng(T + H)
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    r = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
+    want = x.astype(np.float64) @ r.T.astype(np.float64)
+    lg = D.router_logits(cu(x), cu(r)).cpu().numpy()
+    assert np.abs(lg - want).max() <= 2e-6 * np.abs(want).max()
+    logits = torch.empty((T, E), dtype=torch.float32, device="cuda")
+    rexp = torch.empty(T, dtype=torch.int32, device="cuda")
+    idx, w = D.router_route(cu(x), cu(r), k, True, logits=logits, row_exp=rexp)
+    lg2 = logits.cpu().numpy()
+    assert np.array_equal(lg2, lg)                        # the same slice-ordered sums
+    ridx, rw = O.route(lg2, k, True)
+    keep = [t for t in range(T) if t not in set(O.near_ties(lg2, k).tolist())]
+    assert np.array_equal(idx.cpu().numpy()[keep], ridx[keep])
+    np.testing.assert_allclose(w.cpu().numpy()[keep], rw[keep], rtol=2e-6, atol=1e-7)
+    amax = np.abs(x).max(axis=1)
+    assert np.array_equal(rexp.cpu().numpy(), 14 - np.frexp(amax)[1])
+
+
 @pytest.mark.parametrize("case", C.ROUTER_CASES, ids=[c[0] for c in C.ROUTER_CASES])
 def test_permute_matches_group_by_expert(D, golden, case):
     name, T, E, k, norm, seed = case
@@ -272,6 +294,24 @@ def test_qwen_shape_decode_matches_oracle(qwen_layer, T):
     keep = [t for t in range(T) if t not in ties]
     assert np.array_equal(idx[keep], ridx[keep])
     assert layer.status(T) == 0
+
+
+def test_layer_graph_replay_matches_eager(qwen_layer):
+    layer, desc, router, cfg = qwen_layer
+    from distributedmoellm_b200 import synthetic as S
+    x = cu(S.hidden(np.random.default_rng(5), 16, cfg["H"]))
+    eager = layer(x).clone()
+    g = layer.capture(x)
+    x2 = cu(S.hidden(np.random.default_rng(6), 16, cfg["H"]))
+    want2 = layer(x2).clone()
+    x.copy_(x2)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(layer.buffers(16).out, want2)
+    x.copy_(cu(S.hidden(np.random.default_rng(5), 16, cfg["H"])))
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(layer.buffers(16).out, eager)
 
 
 def test_bad_format_raises(D):
