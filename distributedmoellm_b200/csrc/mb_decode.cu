@@ -705,3 +705,58 @@ extern "C" int mb_moe_decode(const MbExpert* table, int E, int H, int I, int gs,
     rc = dispatch_fmt(fmt_down, [&](auto f) { return launch_phase<decltype(f)::value>(a, I, (H + 15) / 16, st); });
     return rc;
 }
+
+// ---- the decode without a caller workspace -----------------------------------
+// Some callers cannot hand the library a workspace: bindings that only forward
+// pointers they were given and have no device allocator of their own, or code
+// running where allocating device memory is not allowed or would fragment a
+// pool it does not own.  For them the decode's scratch (activations, each
+// pick's max |act|, a status word) lives in this array, built into the
+// library: every GPU that loads the library holds MB_NOALLOC_SCRATCH_BYTES of
+// it until the process exits.  All calls share it and it keeps the last
+// call's contents; what must start at zero (the max |act| words) is cleared by
+// every call on the stream before use.
+static __device__ __align__(256) uint8_t g_moe_decode_scratch[MB_NOALLOC_SCRATCH_BYTES];
+
+#include <mutex>
+
+// The array's device address for the current device, looked up once per device
+// (host code may not use the symbol itself as a device address).
+static int noalloc_scratch(void** out)
+{
+    static std::mutex mu;
+    static void* addr[64] = {nullptr};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return mb_fail(MB_ECUDA, "mb_moe_decode_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= 64) return mb_fail(MB_EUNSUPPORTED, "mb_moe_decode_noalloc: device %d", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_moe_decode_scratch);
+        if (e != cudaSuccess || !p)
+            return mb_fail(MB_ECUDA, "mb_moe_decode_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return MB_OK;
+}
+
+extern "C" int mb_moe_decode_noalloc(const MbExpert* table, int E, int H, int I, int gs, int fmt_gu, int fmt_down,
+                                     const float* x, const int32_t* row_exp, int64_t T, const int32_t* counts,
+                                     const int32_t* offsets, const int32_t* sorted_rows, int64_t P, int max_rows,
+                                     float* y, unsigned* status, void* stream)
+{
+    MB_REQUIRE(P >= 0 && I > 0, "mb_moe_decode_noalloc: bad sizes");
+    const int64_t need = mb_moe_decode_workspace_bytes(P, I);
+    if (need > (int64_t)MB_NOALLOC_SCRATCH_BYTES)
+        return mb_fail(MB_EINVAL,
+                       "mb_moe_decode_noalloc: %lld picks with I=%d need %lld bytes of scratch, more than the %lld "
+                       "built into the library; use mb_moe_decode with a workspace",
+                       (long long)P, I, (long long)need, (long long)MB_NOALLOC_SCRATCH_BYTES);
+    void* ws = nullptr;
+    const int rc = noalloc_scratch(&ws);
+    if (rc) return rc;
+    return mb_moe_decode(table, E, H, I, gs, fmt_gu, fmt_down, x, row_exp, T, counts, offsets, sorted_rows, P,
+                         max_rows, y, ws, (int64_t)MB_NOALLOC_SCRATCH_BYTES, status, stream);
+}

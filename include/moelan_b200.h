@@ -139,6 +139,27 @@ int mb_moe_decode(const MbExpert *table, int E, int H, int I, int gs, int fmt_gu
                   const int32_t *sorted_rows, int64_t P, int max_rows, float *y, void *workspace,
                   int64_t workspace_bytes, unsigned *status, void *stream);
 
+/* Size of the scratch array built into the library for mb_moe_decode_noalloc. */
+#define MB_NOALLOC_SCRATCH_BYTES (4 << 20)
+
+/* mb_moe_decode for callers that cannot allocate device memory: those that
+ * have no device allocator of their own (a binding that only forwards the
+ * pointers it is given) or run where allocating is not allowed.  No
+ * counterpart in the reference.  Same arguments and results as mb_moe_decode,
+ * without the workspace: the scratch is a MB_NOALLOC_SCRATCH_BYTES array
+ * inside the library (held on every GPU that loads the library until the
+ * process exits), so mb_moe_decode_workspace_bytes(P, I) must fit in it
+ * (about 1360 picks at I = 768); larger calls fail with MB_EINVAL.  The
+ * call allocates nothing.  The first call on each device looks up the array's
+ * device address (cudaGetSymbolAddress); make that first call before any
+ * stream capture.  All calls share the one array: calls that overlap on the
+ * GPU (other streams, other host threads) race on it and must be ordered by
+ * the caller. */
+int mb_moe_decode_noalloc(const MbExpert *table, int E, int H, int I, int gs, int fmt_gu, int fmt_down,
+                          const float *x, const int32_t *row_exp, int64_t T, const int32_t *counts,
+                          const int32_t *offsets, const int32_t *sorted_rows, int64_t P, int max_rows, float *y,
+                          unsigned *status, void *stream);
+
 /* Workspace bytes for mb_matmul_t with n input rows. */
 int64_t mb_matmul_t_workspace_bytes(int64_t n);
 
