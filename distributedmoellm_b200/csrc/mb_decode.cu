@@ -39,7 +39,6 @@ namespace {
 
 constexpr int kMaxKW = 16;      // MMA warps: one per quad (128 columns) of K, so K <= 2048
 constexpr int kEpiWarps = 2;    // epilogue warps, taking alternate items
-constexpr int kThreadsMax = (kMaxKW + 1 + kEpiWarps) * 32;
 constexpr int kMaxMT = 4;       // row tiles per stage
 constexpr int kRedTile = 128;   // floats of one warp's partial of one tile: [8 input rows][16 rows]
 

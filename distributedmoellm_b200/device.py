@@ -178,6 +178,22 @@ def moe_decode(table: torch.Tensor, E: int, H: int, I: int, gs: int, fmt_gu: int
     return y
 
 
+def prefill_workspace_bytes(P: int, H: int, I: int) -> int:
+    return int(lib().mb_moe_prefill_workspace_bytes(P, H, I))
+
+
+def moe_prefill(table: torch.Tensor, w_exp: torch.Tensor | None, E: int, H: int, I: int, gs: int, fmt_gu: int,
+                fmt_down: int, x: torch.Tensor, row_exp: torch.Tensor, r: Routing, y: torch.Tensor,
+                workspace: torch.Tensor, min_rows: int = 1, status: torch.Tensor | None = None):
+    """Experts with at least ``min_rows`` picks as grouped GEMMs (f16 tensor cores, f32 accumulation)."""
+    _cuda(table, w_exp, x, row_exp, y, workspace, status)
+    check(lib().mb_moe_prefill(_p(table), _p(w_exp), E, H, I, gs, fmt_gu, fmt_down, _p(x), _p(row_exp), x.shape[0],
+                               _p(r.counts), _p(r.offsets), _p(r.sorted_rows), r.P, int(min_rows), _p(y),
+                               _p(workspace), workspace.numel() * workspace.element_size(), _p(status), _stream()),
+          "mb_moe_prefill")
+    return y
+
+
 def matmul_t(w_tiles: torch.Tensor, fmt: int, O: int, K: int, x: torch.Tensor, y: torch.Tensor | None = None,
              workspace: torch.Tensor | None = None, status: torch.Tensor | None = None):
     """x @ W.T for one matrix in the tile layout."""

@@ -30,17 +30,33 @@ class _Buffers:
         self.rws = torch.empty(D.router_workspace_bytes(T, H, E), dtype=torch.uint8, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.out = torch.empty((T, H), dtype=torch.float32, device=dev)
+        self.pws = None     # grouped-GEMM workspace, made on first use
 
 
 class MoELayer:
-    """``router`` (E, H) f32 on the device; ``experts`` the layer's packed experts."""
+    """``router`` (E, H) f32 on the device; ``experts`` the layer's packed experts.
 
-    def __init__(self, router: torch.Tensor, experts: LayerExperts, top_k: int, normalize: bool = True):
+    Experts picked by at least ``gemm_min_rows`` tokens run as grouped GEMMs
+    on the tensor cores (f16 operands, f32 accumulation; the reference's
+    dense path for 8 or more rows, experts.py:148-151, 216-219), the rest
+    through the f32-exact decode mat-vecs.  The GEMM kernels are launched
+    only when the layer's picks average at least half that many per expert
+    (prefill-sized batches) and the shape allows them (H % 128, I % 64);
+    ``gemm_min_rows=0`` keeps every expert on the decode kernels."""
+
+    def __init__(self, router: torch.Tensor, experts: LayerExperts, top_k: int, normalize: bool = True,
+                 gemm_min_rows: int = 32):
         self.router = router.contiguous()
         self.experts = experts
         self.E, self.H, self.I = experts.E, experts.H, experts.I
         self.k, self.normalize = top_k, normalize
+        self.gemm_min_rows = int(gemm_min_rows)
         self._bufs: dict[int, _Buffers] = {}
+
+    def uses_gemm(self, T: int) -> bool:
+        m = self.gemm_min_rows
+        return (m > 0 and self.H % 128 == 0 and self.I % 64 == 0 and 2 * T * self.k >= self.E * m
+                and T * self.k <= 65535)
 
     def buffers(self, T: int) -> _Buffers:
         b = self._bufs.get(T)
@@ -56,8 +72,18 @@ class MoELayer:
 
     def experts_forward(self, x: torch.Tensor, b: _Buffers) -> None:
         ex = self.experts
-        D.moe_decode(ex.table, self.E, self.H, self.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, b.row_exp, b.routing,
-                     b.y, b.ws, max_rows=0, status=b.status)
+        T = x.shape[0]
+        if self.uses_gemm(T):
+            if b.pws is None:
+                b.pws = torch.empty(D.prefill_workspace_bytes(T * self.k, self.H, self.I), dtype=torch.uint8,
+                                    device=x.device)
+            D.moe_decode(ex.table, self.E, self.H, self.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, b.row_exp, b.routing,
+                         b.y, b.ws, max_rows=self.gemm_min_rows - 1, status=b.status)
+            D.moe_prefill(ex.table, ex.wexp, self.E, self.H, self.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, b.row_exp,
+                          b.routing, b.y, b.pws, min_rows=self.gemm_min_rows, status=b.status)
+        else:
+            D.moe_decode(ex.table, self.E, self.H, self.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, b.row_exp, b.routing,
+                         b.y, b.ws, max_rows=0, status=b.status)
 
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """out (T, H) = sum over each token's k picks of weight * expert(x)."""

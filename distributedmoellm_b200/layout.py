@@ -150,6 +150,18 @@ def q8_0_as_q8(raw: np.ndarray, cols: int):
     return q, d
 
 
+def weight_exponent(s, qmax: int) -> int:
+    """The power-of-two exponent e that maps a matrix whose weights are at
+    most qmax * max|s| in magnitude into [2^13, 2^14) (0 for an all-zero or
+    non-finite bound): the tensor-core path multiplies the weights by 2^e
+    before rounding them to f16, and the accumulators by 2^-e after."""
+    amax = float(np.max(np.abs(np.asarray(s, np.float32)))) * qmax if np.size(s) else 0.0
+    if not (0.0 < amax < 3.0e38):
+        return 0
+    _, ex = np.frexp(np.float32(amax))
+    return int(min(120, max(-120, 14 - int(ex))))
+
+
 def q4_0_as_q4(raw: np.ndarray, cols: int):
     """GGUF Q4_0 rows (O, cols/32 * 18) -> (colibri-order offset nibbles (O,
     cols/2), f16 scales (O, cols/32)).  Q4_0 keeps a block's first 16 values

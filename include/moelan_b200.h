@@ -30,8 +30,8 @@ enum {
     MB_EDEVICE = 4       /* a kernel reported a failure in its status word */
 };
 
-/* Weight formats of the device tile layout (see mb_*_relayout in the Python
- * package and the layout notes in DESIGN.md of the repository). */
+/* Weight formats of the device tile layout (16-row tiles of 128-column quads,
+ * built by distributedmoellm_b200/layout.py). */
 enum {
     MB_FMT_Q4_F32 = 1, /* int4, two nibbles per byte, group scales f32 */
     MB_FMT_Q4_F16 = 2, /* int4, group scales f16 */
@@ -159,6 +159,29 @@ int mb_moe_decode_noalloc(const MbExpert *table, int E, int H, int I, int gs, in
                           const float *x, const int32_t *row_exp, int64_t T, const int32_t *counts,
                           const int32_t *offsets, const int32_t *sorted_rows, int64_t P, int max_rows, float *y,
                           unsigned *status, void *stream);
+
+/* ---- prefill: grouped GEMMs on the tensor cores ---------------------------------- */
+
+/* Workspace bytes for mb_moe_prefill with P picks. */
+int64_t mb_moe_prefill_workspace_bytes(int64_t P, int H, int I);
+
+/* One MoE layer's routed experts for experts picked by at least min_rows
+ * tokens (prefill), as grouped GEMMs (tcgen05, f16 operands, f32
+ * accumulation): moelan/experts.py:148-151 and 216-219 (matmul_t with 8 or
+ * more rows: widen the matrix to f32, x @ W.T), run per expert by
+ * ExpertStore.compute (experts.py:707-727) as gate|up, SiLU(gate) * up,
+ * down.  Same tables, routing, row_exp and y (P, H) as mb_moe_decode;
+ * experts with fewer than min_rows picks are left to mb_moe_decode
+ * (max_rows = min_rows - 1).  w_exp (E, 2) int32 (may be NULL = 0): per
+ * expert, the power-of-two exponents that bring the largest weight of its
+ * gate|up and down matrices into [2^13, 2^14) before rounding to f16.
+ * Results agree with the f32 reference within 2e-3 of each output row's
+ * largest magnitude.  Needs H % 128 == 0, I % 64 == 0, P <= 65535, x and
+ * workspace 16-byte aligned. */
+int mb_moe_prefill(const MbExpert *table, const int32_t *w_exp, int E, int H, int I, int gs, int fmt_gu,
+                   int fmt_down, const float *x, const int32_t *row_exp, int64_t T, const int32_t *counts,
+                   const int32_t *offsets, const int32_t *sorted_rows, int64_t P, int min_rows, float *y,
+                   void *workspace, int64_t workspace_bytes, unsigned *status, void *stream);
 
 /* Workspace bytes for mb_matmul_t with n input rows. */
 int64_t mb_matmul_t_workspace_bytes(int64_t n);
