@@ -125,6 +125,29 @@ __device__ __forceinline__ bool mb_mbar_wait(uint64_t* bar, uint32_t parity, uns
     }
 }
 
+// mb_mbar_wait for tight hand-offs: polls try_wait (which itself parks the
+// thread in hardware for a short while) without sleeping in between, reading
+// the timer and the abort flag every 1024 polls; same bound and status.
+__device__ __forceinline__ bool mb_mbar_wait_spin(uint64_t* bar, uint32_t parity, unsigned* status,
+                                                  volatile int* abort_flag)
+{
+    uint64_t t0 = 0;
+    for (uint32_t i = 1;; ++i) {
+        if (mb_mbar_try_wait(bar, parity)) return true;
+        if ((i & 1023u) == 0) {
+            if (*abort_flag) return false;
+            const uint64_t now = mb_globaltimer();
+            if (t0 == 0) {
+                t0 = now;
+            } else if (now - t0 > MB_WAIT_LIMIT_NS) {
+                atomicOr(status, MB_STATUS_TIMEOUT);
+                *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+
 // Global -> shared bulk copy on the TMA engine, completing `bytes` on `bar`.
 // dst, src 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void mb_bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
@@ -198,6 +221,13 @@ __device__ __forceinline__ uint32_t mb_hfma2(uint32_t a, uint32_t b, uint32_t c)
 {
     uint32_t r;
     asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t mb_hmul2(uint32_t a, uint32_t b)
+{
+    uint32_t r;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
     return r;
 }
 

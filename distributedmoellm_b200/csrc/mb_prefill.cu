@@ -5,27 +5,37 @@
 // matmul_t with 8 or more rows: widen the matrix to f32, then BLAS x @ W.T),
 // run per expert by ExpertStore.compute (experts.py:707-727).
 //
-// Design (sm_100a), per CTA = (expert, 128 weight rows), all its tokens:
-//  * the packed weight tiles (the same HBM tile layout the decode kernels read)
-//    are streamed into shared memory with 1-D bulk copies;
-//  * four "dequant" warps turn them into f16 ((q - offset) * group scale in
-//    f32, times the matrix's power-of-two weight exponent, rounded once) and
-//    write them with tcgen05.st straight into tensor memory, where
-//    tcgen05.mma reads its A operand: the converted weights never pass
-//    through shared memory, whose bandwidth the B operand needs;
-//  * the expert's tokens, gathered once per layer into an f16 matrix in pick
-//    order (each row times 2^row exponent, so its largest value lies in
-//    [2^13, 2^14)), arrive as B by 2-D TMA (128-byte swizzle, K-major);
-//  * one thread issues tcgen05.mma (M=128, N <= 192 tokens, K=16, f32 in TMEM);
-//    completions are tracked with tcgen05.commit on mbarriers, every wait is
-//    bounded;
-//  * the same four warps read the accumulators back (tcgen05.ld), undo the
-//    power-of-two scalings exactly and form SiLU(gate) * up in f32 (gate|up)
-//    or the f32 output rows (down).  The activations go through one more
-//    small kernel that rounds each pick's row to f16 with its own exponent.
-// f16 rather than bf16 operands: the same tensor-core rate, 3 more mantissa
-// bits, and with the exponents above no range is lost.  Tolerance against
-// the f32 reference: 2e-3 of each row's max (bf16 operands would give ~7e-3).
+// Two launches per layer (gate|up -> activations, down -> y) of one
+// persistent, warp-specialised kernel: one CTA per SM walks work items
+// (expert, block of 128 weight rows) with
+//  * a weight producer warp: the packed tiles (the same HBM tile layout the
+//    decode kernels read) in 1-D bulk copies into a shared-memory ring;
+//  * a token producer warp: the expert's tokens, gathered once per layer
+//    into an f16 matrix in pick order, as 2-D TMA boxes (128-byte swizzle,
+//    K-major) into a second ring;
+//  * eight dequant warps: (q - offset) * group scale * 2^w in packed f16x2
+//    arithmetic (exact until the one rounding of the product), written with
+//    tcgen05.st straight into tensor memory, where tcgen05.mma reads its A
+//    operand (the converted weights never pass through shared memory);
+//  * one MMA thread: tcgen05.mma M=128, N <= 192 tokens, K=16, f32
+//    accumulators in TMEM, two accumulator buffers;
+//  * four epilogue warps: tcgen05.ld, undo the power-of-two scalings, form
+//    SiLU(gate) * up (written as f16 for the down GEMM) or the f32 output
+//    rows, overlapped with the next item's main loop.
+// Every wait is bounded (status word + abort flag); TMEM is freed on exit.
+//
+// Range scaling (all by powers of two, so exact): a token row is multiplied
+// by 2^row_exp (its largest value in [2^13, 2^14)); a weight matrix by
+// 2^w_exp (its largest possible value in [2^13, 2^14)); a pick's activation
+// row by 2^(a_exp + 2 row_exp), where a_exp comes from the bound
+// |SiLU(g) u| <= max|x|^2 * max_j |Wg_j|_1 * max_j |Wu_j|_1, keeping it
+// below 2^15.  f16 rather than bf16 operands: the same tensor-core rate and
+// 3 more mantissa bits; results agree with the f32 reference within 2e-3 of
+// each row's max (bf16 operands would give ~7e-3).
+//
+// K order: within every 8 columns the f16 operands hold the columns in the
+// order 0 4 1 5 2 6 3 7 (both A and B, so the products are unchanged); it is
+// the order in which the packed nibbles / bytes unpack into f16 pairs.
 #include <cuda.h>
 
 #include <mutex>
@@ -34,33 +44,39 @@
 
 namespace {
 
-constexpr int kBM = 128;      // weight rows per CTA = TMEM lanes
-constexpr int kBK = 64;       // K per chunk: one 128-byte swizzled row of f16
-constexpr int kMaxN = 192;    // tokens per pass
-constexpr int kBStages = 3;   // token (B) chunk stages
-constexpr int kPStages = 2;   // packed-weight stages, one 128-column quad each (two K chunks)
-constexpr int kTmemCols = 256;
-constexpr int kAccCol = 64;   // accumulators at TMEM columns [64, 64 + N); A buffers at [0, 64)
-constexpr int kThreads = 192; // warp 0 TMA, warp 1 MMA + TMEM owner, warps 2..5 dequant / epilogue
+constexpr int kBM = 128;       // weight rows per item = TMEM lanes
+// The K loop runs in quads of 128 columns (two 64-column halves, each one
+// 128-byte swizzle atom of f16), the unit of every hand-off.
+constexpr int kMaxN = 192;     // tokens per pass
+constexpr int kBStages = 3;    // token (B) quad stages: [2 halves][kMaxN rows][128 B] = 48 KB each
+constexpr int kPStages = 4;    // packed-weight stages, one quad of 8 row tiles each
+constexpr int kASlots = 2;     // A (dequantised quad) slots in TMEM, 64 columns each, one per dequant set
+constexpr int kAccCol = kASlots * 64;
+constexpr int kTmemCols = 512;
+static_assert(kAccCol + 2 * kMaxN <= kTmemCols, "TMEM columns");
+constexpr int kDqWarps = 8;    // warps 4..11: two sets of four (one per TMEM lane quarter), alternate quads
+constexpr int kEpiWarps = 4;   // warps 12..15
+constexpr int kThreads = 512;
+constexpr int kBHalf = kMaxN * 128;   // bytes of one half (64 columns) of a token stage
 
 struct PrefillArgs {
     const MbExpert* table;
-    const int32_t* w_exp;   // (E, 2) weight exponents [gate|up, down], or null (0)
+    const int32_t* e_exp;      // (E, 4): gate|up weight exponent, down weight exponent, activation exponent base
     int E;
-    int phase;              // 1: gate|up -> act (f32), 2: down -> y (f32)
-    int NQ;                 // quads of K in the weight tiles
-    int KC;                 // K chunks (K / 64)
-    int RT;                 // row tiles of the matrix
-    int MB;                 // M blocks (8 row tiles) per expert
+    int phase;                 // 1: gate|up -> act (f16), 2: down -> y (f32)
+    int NQ;                    // quads of K in the weight tiles (ceil(K / 128))
+    int KH;                    // 64-column halves of K (K / 64)
+    int RT;                    // row tiles of the matrix
+    int MB;                    // M blocks (8 row tiles) per expert
     int block_bytes;
     const int32_t* counts;
     const int32_t* offsets;
-    const int32_t* tok_rows; // phase 1: sorted_rows (exponent of pick p = tok_exp[tok_rows[p]]); phase 2: null
-    const int32_t* tok_exp;  // phase 1: row exponents of x; phase 2: pick exponents of the activations
+    const int32_t* sorted_rows;
+    const int32_t* row_exp;    // exponents of the rows of x
     int min_rows;
-    int O_real;             // phase 1: I (act columns); phase 2: H (y columns)
-    float* out;             // phase 1: act (P, I); phase 2: y (P, H)
-    int out_ld;
+    int O_real;                // phase 1: I (act columns); phase 2: H (y columns)
+    __half* act;               // phase 1 output (P, I), K-permuted
+    float* y;                  // phase 2 output (P, H)
     unsigned* status;
 };
 
@@ -98,8 +114,28 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint
         : "memory");
 }
 
-// 32 consecutive 32-bit TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32])
+// The same two, issued by one elected lane of a converged warp (the whole warp
+// runs the MMA loop, so descriptors and addresses stay warp-uniform).
+__device__ __forceinline__ void tc_mma_ts_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t.reg .b32 r;\n\telect.sync r|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit_elect(uint64_t* bar)
+{
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\telect.sync r|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(mb_smem_addr(bar))
+        : "memory");
+}
+
+// 32 consecutive 32-bit TMEM columns of this thread's lane (no wait).
+__device__ __forceinline__ void tmem_st32_nowait(uint32_t taddr, const uint32_t (&v)[32])
 {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -108,6 +144,18 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32
         "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]),
         "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]),
         "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 16 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16])
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
         : "memory");
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -159,6 +207,33 @@ __device__ __forceinline__ uint32_t pack_f16(float lo, float hi)
 // 2^e for -126 <= e <= 127, exact.
 __device__ __forceinline__ float pow2i(int e) { return __int_as_float((e + 127) << 23); }
 
+__device__ __forceinline__ int clamp120(int e) { return e < -120 ? -120 : (e > 120 ? 120 : e); }
+
+// The static sequence of work items every role of a CTA walks: items
+// blockIdx.x, blockIdx.x + gridDim.x, ... of E * MB, skipping experts
+// outside this launch.
+struct Items {
+    const PrefillArgs& a;
+    int it;
+    int e, mb, n_e, off_e, passes;
+    __device__ explicit Items(const PrefillArgs& args) : a(args), it((int)blockIdx.x - (int)gridDim.x) {}
+    __device__ bool next()
+    {
+        for (;;) {
+            it += gridDim.x;
+            if (it >= a.E * a.MB) return false;
+            e = it / a.MB;
+            mb = it - e * a.MB;
+            n_e = a.counts[e];
+            if (n_e >= a.min_rows && n_e > 0) {
+                off_e = a.offsets[e];
+                passes = (n_e + kMaxN - 1) / kMaxN;
+                return true;
+            }
+        }
+    }
+};
+
 // ---- the GEMM kernel ----------------------------------------------------------------
 
 template <int FMT>
@@ -169,28 +244,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr bool F16S = (FMT == MB_FMT_Q4_F16 || FMT == MB_FMT_Q8_F16);
     constexpr int kData = Q8 ? 2048 : 1024;
 
-    const int e = blockIdx.x / a.MB, mb = blockIdx.x - e * a.MB;
-    const int n_e = a.counts[e];
-    if (n_e < a.min_rows || n_e <= 0) return;
-    const int off_e = a.offsets[e];
-    const int tiles = min(8, a.RT - mb * 8);     // row tiles of this M block
-    const int wexp = a.w_exp ? a.w_exp[2 * e + (a.phase == 1 ? 0 : 1)] : 0;
-
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint8_t* bst = smem;                                       // [kBStages][kMaxN][128 B]
-    uint8_t* pst = bst + kBStages * kMaxN * 128;               // [kPStages][8 tiles][block]
-    float* tok_scale = reinterpret_cast<float*>(pst + kPStages * 8 * a.block_bytes);   // [2][kMaxN]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(tok_scale + 2 * kMaxN);
+    uint8_t* bst = smem;                                       // [kBStages][2 halves][kMaxN][128 B]
+    uint8_t* pst = bst + kBStages * 2 * kBHalf;                // [kPStages][8 tiles][block]
+    float* tok_s = reinterpret_cast<float*>(pst + kPStages * 8 * a.block_bytes);   // [2][kMaxN] row scale
+    float* tok_a = tok_s + 2 * kMaxN;                          // [2][kMaxN] activation scale (phase 1)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(tok_a + 2 * kMaxN);
     uint64_t* b_full = bars;                                   // [kBStages]
     uint64_t* b_empty = b_full + kBStages;
     uint64_t* p_full = b_empty + kBStages;                     // [kPStages]
     uint64_t* p_empty = p_full + kPStages;
-    uint64_t* a_full = p_empty + kPStages;                     // [2] A buffers in TMEM
-    uint64_t* a_empty = a_full + 2;
-    uint64_t* acc_full = a_empty + 2;
-    uint64_t* acc_empty = acc_full + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+    uint64_t* a_full = p_empty + kPStages;                     // [kASlots]
+    uint64_t* a_empty = a_full + kASlots;
+    uint64_t* acc_full = a_empty + kASlots;                    // [2]
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -203,102 +272,121 @@ __global__ void __launch_bounds__(kThreads, 1)
             mb_mbar_init(&p_full[i], 1);
             mb_mbar_init(&p_empty[i], 4);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < kASlots; ++i) {
             mb_mbar_init(&a_full[i], 4);
             mb_mbar_init(&a_empty[i], 1);
         }
-        mb_mbar_init(acc_full, 1);
-        mb_mbar_init(acc_empty, 4);
+        for (int i = 0; i < 2; ++i) {
+            mb_mbar_init(&acc_full[i], 1);
+            mb_mbar_init(&acc_empty[i], kEpiWarps);
+        }
         *abort_flag = 0;
         mb_fence_mbar_init();
     }
-    if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+    if (warp == 2) tmem_alloc(tmem_slot, kTmemCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    const int KH = a.KH;
+    const int quads = (KH + 1) >> 1;   // quads per pass; the last one has one half when KH is odd
 
-    const int passes = (n_e + kMaxN - 1) / kMaxN;
-    const int KC = a.KC;
-
+    // Every role counts quads gq over all its items and passes: weight stage gq % kPStages, A slot gq % 2
+    // (dequant set gq % 2), token stage gq % kBStages.
     if (warp == 0) {
-        // ------------------------------------------------------------ TMA producer
+        // ------------------------------------------------------------ weight producer
         if (lane == 0) {
-            const uint8_t* wbase =
-                reinterpret_cast<const uint8_t*>(a.phase == 1 ? a.table[e].gu : a.table[e].down);
-            int bs = 0, ps = 0;
-            uint32_t bph = 0, pph = 0;
-            int64_t bn = 0, pn = 0;
-            for (int pass = 0; pass < passes && !*abort_flag; ++pass) {
-                const int n0 = pass * kMaxN;
-                const int nrows = min(kMaxN, n_e - n0);
-                const int nbox = (((nrows + 15) & ~15) + 63) / 64;
-                for (int kc = 0; kc < KC; ++kc) {
-                    if ((kc & 1) == 0) {  // a new quad of packed weights for the M block
-                        if (pn >= kPStages && !mb_mbar_wait(&p_empty[ps], pph ^ 1u, a.status, abort_flag)) break;
+            Items w(a);
+            int64_t gq = 0;
+            while (w.next() && !*abort_flag) {
+                const int tiles = min(8, a.RT - w.mb * 8);
+                const uint8_t* wbase =
+                    reinterpret_cast<const uint8_t*>(a.phase == 1 ? a.table[w.e].gu : a.table[w.e].down);
+                for (int pass = 0; pass < w.passes; ++pass) {
+                    for (int qd = 0; qd < quads; ++qd, ++gq) {
+                        const int ps = (int)(gq % kPStages);
+                        if (gq >= kPStages &&
+                            !mb_mbar_wait_spin(&p_empty[ps], (uint32_t)(((gq / kPStages) - 1) & 1), a.status,
+                                               abort_flag))
+                            break;
                         mb_mbar_arrive_expect_tx(&p_full[ps], (uint32_t)(tiles * a.block_bytes));
                         for (int i = 0; i < tiles; ++i)
                             mb_bulk_g2s(pst + ((size_t)ps * 8 + i) * a.block_bytes,
-                                        wbase + ((size_t)(mb * 8 + i) * a.NQ + (kc >> 1)) * a.block_bytes,
+                                        wbase + ((size_t)(w.mb * 8 + i) * a.NQ + qd) * a.block_bytes,
                                         (uint32_t)a.block_bytes, &p_full[ps]);
-                        ++pn;
-                        if (++ps == kPStages) {
-                            ps = 0;
-                            pph ^= 1u;
-                        }
-                    }
-                    if (bn >= kBStages && !mb_mbar_wait(&b_empty[bs], bph ^ 1u, a.status, abort_flag)) break;
-                    mb_mbar_arrive_expect_tx(&b_full[bs], (uint32_t)(nbox * 64 * 128));
-                    for (int i = 0; i < nbox; ++i)
-                        tma_load_2d(bst + ((size_t)bs * kMaxN + i * 64) * 128, &bmap, kc * kBK, off_e + n0 + i * 64,
-                                    &b_full[bs]);
-                    ++bn;
-                    if (++bs == kBStages) {
-                        bs = 0;
-                        bph ^= 1u;
                     }
                 }
             }
         }
     } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
+        // ------------------------------------------------------------ token producer
         if (lane == 0) {
-            int bs = 0, ab = 0;
-            uint32_t bph = 0, abph = 0;
-            for (int pass = 0; pass < passes && !*abort_flag; ++pass) {
-                const int nrows = min(kMaxN, n_e - pass * kMaxN);
-                const int npad = (nrows + 15) & ~15;
-                const uint32_t idesc = idesc_f16(npad);
-                if (pass > 0 && !mb_mbar_wait(acc_empty, (uint32_t)((pass - 1) & 1), a.status, abort_flag)) break;
-                tc_fence_after();
-                for (int kc = 0; kc < KC; ++kc) {
-                    if (!mb_mbar_wait(&a_full[ab], abph, a.status, abort_flag)) break;
-                    if (!mb_mbar_wait(&b_full[bs], bph, a.status, abort_flag)) break;
-                    tc_fence_after();
-                    const uint32_t bbase = mb_smem_addr(bst + (size_t)bs * kMaxN * 128);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        tc_mma_ts(tmem + kAccCol, tmem + ab * 32 + j * 8, sw128_desc(bbase + j * 32), idesc,
-                                  (kc > 0 || j > 0) ? 1u : 0u);
-                    tc_commit(&a_empty[ab]);
-                    tc_commit(&b_empty[bs]);
-                    if (++ab == 2) {
-                        ab = 0;
-                        abph ^= 1u;
-                    }
-                    if (++bs == kBStages) {
-                        bs = 0;
-                        bph ^= 1u;
+            Items w(a);
+            int64_t gq = 0;
+            while (w.next() && !*abort_flag) {
+                for (int pass = 0; pass < w.passes; ++pass) {
+                    const int n0 = pass * kMaxN;
+                    const int nrows = min(kMaxN, w.n_e - n0);
+                    const int nbox = (((nrows + 15) & ~15) + 63) / 64;
+                    for (int qd = 0; qd < quads; ++qd, ++gq) {
+                        const int bs = (int)(gq % kBStages);
+                        const int nh = min(2, KH - 2 * qd);
+                        if (gq >= kBStages &&
+                            !mb_mbar_wait_spin(&b_empty[bs], (uint32_t)(((gq / kBStages) - 1) & 1), a.status,
+                                               abort_flag))
+                            break;
+                        mb_mbar_arrive_expect_tx(&b_full[bs], (uint32_t)(nh * nbox * 64 * 128));
+                        for (int hh = 0; hh < nh; ++hh)
+                            for (int i = 0; i < nbox; ++i)
+                                tma_load_2d(bst + ((size_t)(bs * 2 + hh) * kMaxN + i * 64) * 128, &bmap,
+                                            qd * 128 + hh * 64, w.off_e + n0 + i * 64, &b_full[bs]);
                     }
                 }
-                tc_commit(acc_full);
             }
         }
-    } else {
-        // ------------------------------------------------------------ dequant + epilogue
+    } else if (warp == 2) {
+        // ------------------------------------------------------------ MMA issuer (whole warp, one lane issues)
+        Items w(a);
+        int64_t gq = 0;
+        int64_t np = 0;   // passes issued (accumulator buffer np & 1)
+        bool ok = true;
+        while (ok && w.next()) {
+            for (int pass = 0; ok && pass < w.passes; ++pass, ++np) {
+                const int nrows = min(kMaxN, w.n_e - pass * kMaxN);
+                const uint32_t idesc = idesc_f16((nrows + 15) & ~15);
+                const int slot = (int)(np & 1);
+                if (np >= 2)
+                    ok = __all_sync(0xffffffffu, mb_mbar_wait_spin(&acc_empty[slot], (uint32_t)(((np >> 1) - 1) & 1),
+                                                                    a.status, abort_flag));
+                tc_fence_after();
+                const uint32_t dcol = tmem + kAccCol + slot * kMaxN;
+                for (int qd = 0; ok && qd < quads; ++qd, ++gq) {
+                    const int as = (int)(gq & 1), bs = (int)(gq % kBStages);
+                    const int nh = min(2, KH - 2 * qd);
+                    ok = __all_sync(0xffffffffu,
+                                    mb_mbar_wait_spin(&a_full[as], (uint32_t)((gq >> 1) & 1), a.status, abort_flag) &&
+                                        mb_mbar_wait_spin(&b_full[bs], (uint32_t)((gq / kBStages) & 1), a.status,
+                                                          abort_flag));
+                    if (!ok) break;
+                    tc_fence_after();
+                    for (int hh = 0; hh < nh; ++hh) {
+                        const uint32_t bbase = mb_smem_addr(bst + (size_t)(bs * 2 + hh) * kBHalf);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            tc_mma_ts_elect(dcol, tmem + as * 64 + hh * 32 + j * 8, sw128_desc(bbase + j * 32),
+                                            idesc, (qd > 0 || hh > 0 || j > 0) ? 1u : 0u);
+                    }
+                    tc_commit_elect(&a_empty[as]);
+                    tc_commit_elect(&b_empty[bs]);
+                }
+                tc_commit_elect(&acc_full[slot]);
+            }
+        }
+    } else if (warp >= 4 && warp < 4 + kDqWarps) {
+        // ------------------------------------------------------------ dequant (two sets, alternate quads)
         const int q = warp & 3;               // TMEM lane quarter this warp may access
+        const int set = (warp - 4) >> 2;      // this set takes the quads gq with gq % 2 == set
         const int L = 32 * q + lane;          // TMEM lane = row of the M block
-        const int et = threadIdx.x - 64;      // 0..127 among the four warps
         int ti, trow;                         // source row tile within the M block, row within it
         if (a.phase == 1) {                   // lanes 32q + s: gate row, 32q + 16 + s: the matching up row
             const int s = lane & 15;
@@ -308,189 +396,209 @@ __global__ void __launch_bounds__(kThreads, 1)
             ti = L >> 4;
             trow = L & 15;
         }
-        const bool row_ok = ti < tiles;
-        const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
-        const float wscale = pow2i(wexp), wunscale = pow2i(-wexp);
-        int ps = 0, ab = 0;
-        uint32_t pph = 0, abph = 0;
-        int64_t an = 0;
-        for (int pass = 0; pass < passes; ++pass) {
-            const int n0 = pass * kMaxN;
-            const int nrows = min(kMaxN, n_e - n0);
-            const int npad = (nrows + 15) & ~15;
-            float* tsc = tok_scale + (pass & 1) * kMaxN;
-            for (int n = et; n < nrows; n += 128) {
-                const int64_t p = off_e + n0 + n;
-                tsc[n] = pow2i(-a.tok_exp[a.tok_rows ? a.tok_rows[p] : p]);
-            }
-            mb_named_barrier(1, 128);
-            for (int kc = 0; kc < KC; ++kc) {
-                const int h = kc & 1;
-                bool ok = true;
-                if (h == 0) ok = mb_mbar_wait(&p_full[ps], pph, a.status, abort_flag);
-                if (an >= 2) ok = mb_mbar_wait(&a_empty[ab], abph ^ 1u, a.status, abort_flag) && ok;
-                tc_fence_after();
-                uint32_t v[32];
-                const uint8_t* blk = pst + ((size_t)ps * 8 + (row_ok ? ti : 0)) * a.block_bytes;
-                float sc[2];
-                if (F16S) {
-                    const __half2 s2 = *reinterpret_cast<const __half2*>(blk + kData + trow * 8 + 4 * h);
-                    sc[0] = __low2float(s2);
-                    sc[1] = __high2float(s2);
-                } else {
-                    const float2 s2 = *reinterpret_cast<const float2*>(blk + kData + trow * 16 + 8 * h);
-                    sc[0] = s2.x;
-                    sc[1] = s2.y;
-                }
-                if (!ok || !row_ok) {
-                    sc[0] = 0.f;
-                    sc[1] = 0.f;
-                }
-                if (!Q8) {
-                    // int4: lane word t holds 4 bytes (8 columns 8t..8t+7, low nibble = even column) of each of
-                    // the quad's groups; this chunk takes groups 2h and 2h+1.  Column pair (8t+2b, 8t+2b+1) of
-                    // group gl is f16 pair 16*gl + 4t + b of the chunk's 64 columns.
-#pragma unroll
-                    for (int t = 0; t < 4; ++t) {
-                        const uint2 wv = *reinterpret_cast<const uint2*>(blk + trow * 64 + t * 16 + 8 * h);
-#pragma unroll
-                        for (int b = 0; b < 4; ++b) {
-                            const uint32_t x0 = (wv.x >> (8 * b)) & 0xFF, x1 = (wv.y >> (8 * b)) & 0xFF;
-                            const float lo0 = __int_as_float(0x4B000000 | (x0 & 15)) - 8388616.0f;
-                            const float hi0 = __int_as_float(0x4B000000 | (x0 >> 4)) - 8388616.0f;
-                            const float lo1 = __int_as_float(0x4B000000 | (x1 & 15)) - 8388616.0f;
-                            const float hi1 = __int_as_float(0x4B000000 | (x1 >> 4)) - 8388616.0f;
-                            v[4 * t + b] = pack_f16(lo0 * sc[0] * wscale, hi0 * sc[0] * wscale);
-                            v[16 + 4 * t + b] = pack_f16(lo1 * sc[1] * wscale, hi1 * sc[1] * wscale);
-                        }
+        const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + set * 64;
+        Items w(a);
+        int64_t gq = 0;
+        while (w.next()) {
+            const int tiles = min(8, a.RT - w.mb * 8);
+            const bool row_ok = ti < tiles;
+            const int wexp = a.e_exp[4 * w.e + (a.phase == 1 ? 0 : 1)];
+            const float wscale = pow2i(clamp120(wexp));
+            for (int pass = 0; pass < w.passes; ++pass) {
+                for (int qd = 0; qd < quads; ++qd, ++gq) {
+                    if ((int)(gq & 1) != set) continue;
+                    const int ps = (int)(gq % kPStages);
+                    const int nh = min(2, KH - 2 * qd);
+                    const int64_t use = gq >> 1;     // uses of this set's A slot so far
+                    bool ok = mb_mbar_wait_spin(&p_full[ps], (uint32_t)((gq / kPStages) & 1), a.status, abort_flag);
+                    if (use >= 1)
+                        ok = mb_mbar_wait_spin(&a_empty[set], (uint32_t)((use - 1) & 1), a.status, abort_flag) && ok;
+                    tc_fence_after();
+                    const uint8_t* blk = pst + ((size_t)ps * 8 + (row_ok ? ti : 0)) * a.block_bytes;
+                    // the quad's four group scales, times 2^wexp, as f16x2 pairs (s, s)
+                    uint32_t s2[4];
+                    if (F16S) {
+                        const uint2 sv = *reinterpret_cast<const uint2*>(blk + kData + trow * 8);
+                        const __half2 h01 = *reinterpret_cast<const __half2*>(&sv.x);
+                        const __half2 h23 = *reinterpret_cast<const __half2*>(&sv.y);
+                        s2[0] = pack_f16(__low2float(h01) * wscale, __low2float(h01) * wscale);
+                        s2[1] = pack_f16(__high2float(h01) * wscale, __high2float(h01) * wscale);
+                        s2[2] = pack_f16(__low2float(h23) * wscale, __low2float(h23) * wscale);
+                        s2[3] = pack_f16(__high2float(h23) * wscale, __high2float(h23) * wscale);
+                    } else {
+                        const float4 sv = *reinterpret_cast<const float4*>(blk + kData + trow * 16);
+                        s2[0] = pack_f16(sv.x * wscale, sv.x * wscale);
+                        s2[1] = pack_f16(sv.y * wscale, sv.y * wscale);
+                        s2[2] = pack_f16(sv.z * wscale, sv.z * wscale);
+                        s2[3] = pack_f16(sv.w * wscale, sv.w * wscale);
                     }
-                } else {
-                    // int8: half h holds groups 2h, 2h+1; lane word t has the 8 columns 8t..8t+7 of each in
-                    // the order c0 c4 c1 c5 c2 c6 c3 c7 (offset by 128).
+                    if (!ok || !row_ok) s2[0] = s2[1] = s2[2] = s2[3] = 0u;
+                    // half hh covers groups 2hh, 2hh+1; TMEM column 32*hh + 16*gl + 4*t + i of the slot holds
+                    // the f16 pair (column 8t+i, column 8t+i+4) of group 2hh+gl.
+                    for (int hh = 0; hh < nh; ++hh) {
+                        uint32_t v[32];
+                        if (!Q8) {
+                            // int4: lane word t holds word t (columns 8t..8t+7, nibble n = column 8t+n,
+                            // u = v + 8) of each of the quad's four groups.
 #pragma unroll
-                    for (int t = 0; t < 4; ++t) {
-                        const uint4 wv = *reinterpret_cast<const uint4*>(blk + h * 1024 + trow * 64 + t * 16);
-                        const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
+                            for (int t = 0; t < 4; ++t) {
+                                const uint2 wv = *reinterpret_cast<const uint2*>(blk + trow * 64 + t * 16 + 8 * hh);
 #pragma unroll
-                        for (int gl = 0; gl < 2; ++gl) {
-                            const uint32_t w0 = w[2 * gl], w1 = w[2 * gl + 1];
-                            // columns (8t+2i, 8t+2i+1) sit at byte positions (0,2) (4,6) (1,3) (5,7)
-                            const uint32_t byt[8] = {w0 & 0xFF, (w0 >> 8) & 0xFF, (w0 >> 16) & 0xFF, w0 >> 24,
-                                                     w1 & 0xFF, (w1 >> 8) & 0xFF, (w1 >> 16) & 0xFF, w1 >> 24};
-                            const int pa[4] = {0, 4, 1, 5}, pb[4] = {2, 6, 3, 7};
+                                for (int gl = 0; gl < 2; ++gl) {
+                                    const uint32_t wd = gl ? wv.y : wv.x, w8 = wd >> 8;
+                                    const uint32_t sg = s2[2 * hh + gl];
+                                    uint32_t* o = v + 16 * gl + 4 * t;
+                                    o[0] = mb_hmul2(mb_hsub2(mb_lop_and_or(wd, 0x000F000Fu, 0x64006400u), 0x64086408u),
+                                                    sg);
+                                    o[1] = mb_hmul2(
+                                        mb_hfma2(mb_lop_and_or(wd, 0x00F000F0u, 0x64006400u), 0x2C002C00u, 0xD480D480u),
+                                        sg);
+                                    o[2] = mb_hmul2(mb_hsub2(mb_lop_and_or(w8, 0x000F000Fu, 0x64006400u), 0x64086408u),
+                                                    sg);
+                                    o[3] = mb_hmul2(
+                                        mb_hfma2(mb_lop_and_or(w8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, 0xD480D480u),
+                                        sg);
+                                }
+                            }
+                        } else {
+                            // int8: half hh holds groups 2hh, 2hh+1; lane word t has the 8 columns 8t..8t+7 of
+                            // each (group 2hh + gl at byte 8 gl), bytes u = q + 128 in the order
+                            // c0 c4 c1 c5 c2 c6 c3 c7: byte pair i is the pair (8t+i, 8t+i+4).
 #pragma unroll
-                            for (int i = 0; i < 4; ++i) {
-                                const float f0 = __int_as_float(0x4B000000 | byt[pa[i]]) - 8388736.0f;
-                                const float f1 = __int_as_float(0x4B000000 | byt[pb[i]]) - 8388736.0f;
-                                v[16 * gl + 4 * t + i] = pack_f16(f0 * sc[gl] * wscale, f1 * sc[gl] * wscale);
+                            for (int t = 0; t < 4; ++t) {
+                                const uint4 wv = *reinterpret_cast<const uint4*>(blk + hh * 1024 + trow * 64 + t * 16);
+#pragma unroll
+                                for (int gl = 0; gl < 2; ++gl) {
+                                    const uint32_t w0 = gl ? wv.z : wv.x, w1 = gl ? wv.w : wv.y;
+                                    const uint32_t sg = s2[2 * hh + gl];
+                                    uint32_t* o = v + 16 * gl + 4 * t;
+                                    o[0] = mb_hmul2(mb_hsub2(mb_prmt(w0, 0x00006464u, 0x5140u), 0x64806480u), sg);
+                                    o[1] = mb_hmul2(mb_hsub2(mb_prmt(w0, 0x00006464u, 0x5342u), 0x64806480u), sg);
+                                    o[2] = mb_hmul2(mb_hsub2(mb_prmt(w1, 0x00006464u, 0x5140u), 0x64806480u), sg);
+                                    o[3] = mb_hmul2(mb_hsub2(mb_prmt(w1, 0x00006464u, 0x5342u), 0x64806480u), sg);
+                                }
                             }
                         }
+                        tmem_st32_nowait(taddr + 32 * hh, v);
+                    }
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mb_mbar_arrive(&a_full[set]);
+                        mb_mbar_arrive(&p_empty[ps]);
                     }
                 }
-                tmem_st32(tmem + lane_addr + ab * 32, v);
-                tc_fence_before();
-                __syncwarp();
-                const bool quad_done = h == 1 || kc == KC - 1;
-                if (lane == 0) {
-                    mb_mbar_arrive(&a_full[ab]);
-                    if (quad_done) mb_mbar_arrive(&p_empty[ps]);
-                }
-                ++an;
-                if (++ab == 2) {
-                    ab = 0;
-                    abph ^= 1u;
-                }
-                if (quad_done && ++ps == kPStages) {
-                    ps = 0;
-                    pph ^= 1u;
-                }
             }
-            // epilogue of this pass
-            const bool ok = mb_mbar_wait(acc_full, (uint32_t)(pass & 1), a.status, abort_flag);
-            tc_fence_after();
-            for (int cb = 0; cb < npad; cb += 32) {
-                uint32_t r[32];
-                tmem_ld32(tmem + lane_addr + kAccCol + cb, r);
-                if (!ok) continue;
-                if (a.phase == 1) {
-                    const int s = lane & 15;
-                    const int j = mb * 64 + 16 * q + s;
+        }
+    } else if (warp >= 4 + kDqWarps) {
+        // ------------------------------------------------------------ epilogue
+        const int q = warp & 3;
+        const int L = 32 * q + lane;
+        const int et = threadIdx.x - 32 * (4 + kDqWarps);   // 0..127
+        const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
+        Items w(a);
+        int64_t np = 0;
+        while (w.next()) {
+            const int* ee = a.e_exp + 4 * w.e;
+            const int wexp = ee[a.phase == 1 ? 0 : 1];
+            const float wunscale = pow2i(-clamp120(wexp));
+            for (int pass = 0; pass < w.passes; ++pass, ++np) {
+                const int slot = (int)(np & 1);
+                const int n0 = pass * kMaxN;
+                const int nrows = min(kMaxN, w.n_e - n0);
+                const int npad = (nrows + 15) & ~15;
+                float* ts = tok_s + slot * kMaxN;
+                float* ta = tok_a + slot * kMaxN;
+                for (int n = et; n < ((nrows + 31) & ~31); n += 128) {   // padding tokens: scale 0
+                    float s0 = 0.f, s1 = 0.f;
+                    if (n < nrows) {
+                        const int rexp = a.row_exp[a.sorted_rows[w.off_e + n0 + n]];
+                        const int ea = clamp120(ee[2] + 2 * rexp);
+                        s0 = pow2i(a.phase == 1 ? -clamp120(rexp) : -ea);
+                        s1 = pow2i(ea);
+                    }
+                    ts[n] = s0;
+                    ta[n] = s1;
+                }
+                mb_named_barrier(1, 32 * kEpiWarps);
+                const bool ok = mb_mbar_wait_spin(&acc_full[slot], (uint32_t)((np >> 1) & 1), a.status, abort_flag);
+                tc_fence_after();
+                const uint32_t acol = tmem + lane_addr + kAccCol + slot * kMaxN;
+                for (int cb = 0; cb < npad; cb += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(acol + cb, r);
+                    if (!ok) continue;
+                    if (a.phase == 1) {
+                        // lanes s < 16 hold gate row j, lanes 16 + s the up row j: per pair of tokens (i, i+1)
+                        // the low lane forms token i and the high lane token i+1; then lanes s and s+4 (columns
+                        // j, j+4: adjacent in the K order) store one f16 pair.
+                        const int s = lane & 15;
+                        const bool hi = lane >= 16;
+                        const int j = w.mb * 64 + 16 * q + s;
+                        const int jpos = (j & ~7) + 2 * (s & 3);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const int n = cb + i;
-                        const float gv = __uint_as_float(r[i]) * tsc[n < kMaxN ? n : 0] * wunscale;
-                        const float uv = __shfl_xor_sync(0xffffffffu, gv, 16);
-                        if (lane < 16 && n < nrows && j < a.O_real) {
-                            const float act = gv / (1.0f + expf(-gv)) * uv;
-                            a.out[(int64_t)(off_e + n0 + n) * a.out_ld + j] = act;
+                        for (int i = 0; i < 32; i += 2) {
+                            const float other =
+                                __uint_as_float(__shfl_xor_sync(0xffffffffu, hi ? r[i] : r[i + 1], 16));
+                            const int n = cb + i + (hi ? 1 : 0);
+                            const float f = ts[n] * wunscale;
+                            const float gv = (hi ? other : __uint_as_float(r[i])) * f;
+                            const float uv = (hi ? __uint_as_float(r[i + 1]) : other) * f;
+                            const float act = __fdividef(gv, 1.0f + __expf(-gv)) * uv * ta[n];
+                            const float act4 = __shfl_xor_sync(0xffffffffu, act, 4);
+                            if ((s & 4) == 0 && n < nrows && j < a.O_real)
+                                *reinterpret_cast<uint32_t*>(a.act + (int64_t)(w.off_e + n0 + n) * a.O_real + jpos) =
+                                    pack_f16(act, act4);
+                        }
+                    } else {
+                        const int o = w.mb * kBM + L;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const int n = cb + i;
+                            if (n < nrows && o < a.O_real)
+                                a.y[(int64_t)(w.off_e + n0 + n) * a.O_real + o] =
+                                    __uint_as_float(r[i]) * ts[n] * wunscale;
                         }
                     }
-                } else {
-                    const int o = mb * kBM + L;
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const int n = cb + i;
-                        if (n < nrows && o < a.O_real)
-                            a.out[(int64_t)(off_e + n0 + n) * a.out_ld + o] =
-                                __uint_as_float(r[i]) * tsc[n] * wunscale;
-                    }
                 }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mb_mbar_arrive(&acc_empty[slot]);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mb_mbar_arrive(acc_empty);
         }
     }
 
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+    if (warp == 2) tmem_dealloc(tmem, kTmemCols);
 }
 
-// The picks' tokens in pick order as f16, each row scaled by 2^row_exp[row]:
-// xp[p] = f16(x[sorted_rows[p]] * 2^row_exp[sorted_rows[p]]).
+// Eight f32 values as four f16 pairs in the K order 0 4 1 5 2 6 3 7.
+__device__ __forceinline__ uint4 pack8_perm(const float4 lo, const float4 hi, float sc)
+{
+    uint4 o;
+    o.x = pack_f16(lo.x * sc, hi.x * sc);
+    o.y = pack_f16(lo.y * sc, hi.y * sc);
+    o.z = pack_f16(lo.z * sc, hi.z * sc);
+    o.w = pack_f16(lo.w * sc, hi.w * sc);
+    return o;
+}
+
+// The picks' tokens in pick order as f16, each row scaled by 2^row_exp[row]
+// (K-permuted): xp[p] = f16(x[sorted_rows[p]] * 2^row_exp[sorted_rows[p]]).
 __global__ void gather_f16_kernel(const float* __restrict__ x, const int32_t* __restrict__ sorted_rows,
                                   const int32_t* __restrict__ row_exp, int64_t P, int H, __half* __restrict__ xp)
 {
     const int64_t p = blockIdx.y;
-    const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
     if (p >= P || c >= H) return;
     const int64_t row = sorted_rows[p];
-    const float sc = pow2i(row_exp[row]);
-    const float4 v = *reinterpret_cast<const float4*>(x + row * H + c);
-    uint2 o;
-    o.x = pack_f16(v.x * sc, v.y * sc);
-    o.y = pack_f16(v.z * sc, v.w * sc);
-    *reinterpret_cast<uint2*>(xp + p * H + c) = o;
-}
-
-// Each pick's activation row to f16 with its own exponent (one warp per pick):
-// e = the exponent that maps the row's largest magnitude into [2^13, 2^14).
-__global__ void act_to_f16_kernel(const float* __restrict__ act, int64_t P, int I, __half* __restrict__ act16,
-                                  int32_t* __restrict__ pick_exp)
-{
-    const int64_t p = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (p >= P) return;
-    const float* row = act + p * I;
-    float m = 0.0f;
-    for (int c = lane * 4; c < I; c += 128) {
-        const float4 v = *reinterpret_cast<const float4*>(row + c);
-        m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const int e = mb_row_exponent(m);
-    const float sc = pow2i(e);
-    for (int c = lane * 4; c < I; c += 128) {
-        const float4 v = *reinterpret_cast<const float4*>(row + c);
-        uint2 o;
-        o.x = pack_f16(v.x * sc, v.y * sc);
-        o.y = pack_f16(v.z * sc, v.w * sc);
-        *reinterpret_cast<uint2*>(act16 + p * I + c) = o;
-    }
-    if (lane == 0) pick_exp[p] = e;
+    const float sc = pow2i(clamp120(row_exp[row]));
+    const float4 lo = *reinterpret_cast<const float4*>(x + row * H + c);
+    const float4 hi = *reinterpret_cast<const float4*>(x + row * H + c + 4);
+    *reinterpret_cast<uint4*>(xp + p * H + c) = pack8_perm(lo, hi, sc);
 }
 
 // ---- host side -----------------------------------------------------------------------
@@ -542,8 +650,8 @@ int block_bytes_of(int fmt)
 
 size_t smem_bytes(int block_bytes)
 {
-    return 1024 + (size_t)kBStages * kMaxN * 128 + (size_t)kPStages * 8 * block_bytes + 2 * kMaxN * 4 + 16 * 8 +
-           64;
+    return 1024 + (size_t)kBStages * 2 * kBHalf + (size_t)kPStages * 8 * block_bytes + 4 * kMaxN * 4 +
+           (2 * kBStages + 2 * kPStages + 2 * kASlots + 4) * 8 + 64;
 }
 
 template <int FMT>
@@ -559,7 +667,9 @@ int launch(const PrefillArgs& a, const CUtensorMap& map, cudaStream_t st)
         if (e != cudaSuccess) return mb_fail(MB_ECUDA, "mb_moe_prefill: smem attribute: %s", cudaGetErrorString(e));
         set[dev & 63] = smem;
     }
-    kern<<<a.E * a.MB, kThreads, smem, st>>>(a, map);
+    const int items = a.E * a.MB;
+    const int grid = items < mb_num_sms() ? items : mb_num_sms();
+    kern<<<grid, kThreads, smem, st>>>(a, map);
     return mb_check_launch("mb_moe_prefill");
 }
 
@@ -578,19 +688,19 @@ int64_t r1k(int64_t n) { return (n + 1023) / 1024 * 1024; }
 
 }  // namespace
 
-// Workspace (from its first 1024-byte boundary): the picks' tokens as f16 (P x H) | the activations in f32
-// (P x I) | the activations as f16 (P x I) | each pick's activation exponent (P) | status word.
+// Workspace (from its first 1024-byte boundary): the picks' tokens as f16 (P x H) | the activations as f16
+// (P x I) | status word.
 extern "C" int64_t mb_moe_prefill_workspace_bytes(int64_t P, int H, int I)
 {
-    return 1024 + r1k(P * H * 2) + r1k(P * I * 4) + r1k(P * I * 2) + r1k(P * 4) + 256;
+    return 1024 + r1k(P * H * 2) + r1k(P * I * 2) + 256;
 }
 
-extern "C" int mb_moe_prefill(const MbExpert* table, const int32_t* w_exp, int E, int H, int I, int gs, int fmt_gu,
+extern "C" int mb_moe_prefill(const MbExpert* table, const int32_t* e_exp, int E, int H, int I, int gs, int fmt_gu,
                               int fmt_down, const float* x, const int32_t* row_exp, int64_t T, const int32_t* counts,
                               const int32_t* offsets, const int32_t* sorted_rows, int64_t P, int min_rows, float* y,
                               void* workspace, int64_t workspace_bytes, unsigned* status, void* stream)
 {
-    MB_REQUIRE(table && x && row_exp && counts && offsets && sorted_rows && y && workspace,
+    MB_REQUIRE(table && e_exp && x && row_exp && counts && offsets && sorted_rows && y && workspace,
                "mb_moe_prefill: null pointer");
     MB_REQUIRE(E > 0 && E <= 65535 && T >= 0 && P >= 0, "mb_moe_prefill: bad sizes");
     MB_REQUIRE(H % 128 == 0 && I % 64 == 0 && H > 0 && I > 0,
@@ -605,66 +715,53 @@ extern "C" int mb_moe_prefill(const MbExpert* table, const int32_t* w_exp, int E
     uint8_t* ws = reinterpret_cast<uint8_t*>(((uintptr_t)workspace + 1023) & ~(uintptr_t)1023);
     __half* xp = reinterpret_cast<__half*>(ws);
     ws += r1k(P * H * 2);
-    float* act32 = reinterpret_cast<float*>(ws);
-    ws += r1k(P * I * 4);
-    __half* act16 = reinterpret_cast<__half*>(ws);
+    __half* act = reinterpret_cast<__half*>(ws);
     ws += r1k(P * I * 2);
-    int32_t* pick_exp = reinterpret_cast<int32_t*>(ws);
-    ws += r1k(P * 4);
-    unsigned* ws_status = reinterpret_cast<unsigned*>(ws);
     if (!status) {
-        status = ws_status;
+        status = reinterpret_cast<unsigned*>(ws);
         cudaMemsetAsync(status, 0, sizeof(unsigned), st);
     }
 
-    gather_f16_kernel<<<dim3((H / 4 + 255) / 256, (unsigned)P), 256, 0, st>>>(x, sorted_rows, row_exp, P, H, xp);
+    gather_f16_kernel<<<dim3((H / 8 + 127) / 128, (unsigned)P), 128, 0, st>>>(x, sorted_rows, row_exp, P, H, xp);
     int rc = mb_check_launch("mb_moe_prefill gather");
     if (rc) return rc;
 
     PrefillArgs a{};
     a.table = table;
-    a.w_exp = w_exp;
+    a.e_exp = e_exp;
     a.E = E;
     a.counts = counts;
     a.offsets = offsets;
+    a.sorted_rows = sorted_rows;
+    a.row_exp = row_exp;
     a.min_rows = min_rows < 1 ? 1 : min_rows;
     a.status = status;
+    a.act = act;
+    a.y = y;
 
     CUtensorMap map;
-    // gate|up: K = H, rows 2I (RT = I/8 tiles of 8 gate + 8 up rows) -> act (P, I) f32
+    // gate|up: K = H, rows 2I (RT = I/8 tiles of 8 gate + 8 up rows) -> act (P, I) f16
     rc = f16_map(&map, xp, P, H);
     if (rc) return rc;
     a.phase = 1;
     a.NQ = H / 128;
-    a.KC = H / kBK;
+    a.KH = H / 64;
     a.RT = I / 8;
     a.MB = (a.RT + 7) / 8;
     a.block_bytes = block_bytes_of(fmt_gu);
-    a.tok_rows = sorted_rows;
-    a.tok_exp = row_exp;
     a.O_real = I;
-    a.out = act32;
-    a.out_ld = I;
     rc = dispatch(fmt_gu, a, map, st);
     if (rc) return rc;
 
-    act_to_f16_kernel<<<(unsigned)((P + 7) / 8), 256, 0, st>>>(act32, P, I, act16, pick_exp);
-    rc = mb_check_launch("mb_moe_prefill act");
-    if (rc) return rc;
-
     // down: K = I, rows H -> y (P, H)
-    rc = f16_map(&map, act16, P, I);
+    rc = f16_map(&map, act, P, I);
     if (rc) return rc;
     a.phase = 2;
     a.NQ = (I + 127) / 128;
-    a.KC = I / kBK;
+    a.KH = I / 64;
     a.RT = H / 16;
     a.MB = (a.RT + 7) / 8;
     a.block_bytes = block_bytes_of(fmt_down);
-    a.tok_rows = nullptr;
-    a.tok_exp = pick_exp;
     a.O_real = H;
-    a.out = y;
-    a.out_ld = H;
     return dispatch(fmt_down, a, map, st);
 }

@@ -182,12 +182,12 @@ def prefill_workspace_bytes(P: int, H: int, I: int) -> int:
     return int(lib().mb_moe_prefill_workspace_bytes(P, H, I))
 
 
-def moe_prefill(table: torch.Tensor, w_exp: torch.Tensor | None, E: int, H: int, I: int, gs: int, fmt_gu: int,
+def moe_prefill(table: torch.Tensor, e_exp: torch.Tensor, E: int, H: int, I: int, gs: int, fmt_gu: int,
                 fmt_down: int, x: torch.Tensor, row_exp: torch.Tensor, r: Routing, y: torch.Tensor,
                 workspace: torch.Tensor, min_rows: int = 1, status: torch.Tensor | None = None):
     """Experts with at least ``min_rows`` picks as grouped GEMMs (f16 tensor cores, f32 accumulation)."""
-    _cuda(table, w_exp, x, row_exp, y, workspace, status)
-    check(lib().mb_moe_prefill(_p(table), _p(w_exp), E, H, I, gs, fmt_gu, fmt_down, _p(x), _p(row_exp), x.shape[0],
+    _cuda(table, e_exp, x, row_exp, y, workspace, status)
+    check(lib().mb_moe_prefill(_p(table), _p(e_exp), E, H, I, gs, fmt_gu, fmt_down, _p(x), _p(row_exp), x.shape[0],
                                _p(r.counts), _p(r.offsets), _p(r.sorted_rows), r.P, int(min_rows), _p(y),
                                _p(workspace), workspace.numel() * workspace.element_size(), _p(status), _stream()),
           "mb_moe_prefill")

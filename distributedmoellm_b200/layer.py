@@ -56,7 +56,7 @@ class MoELayer:
     def uses_gemm(self, T: int) -> bool:
         m = self.gemm_min_rows
         return (m > 0 and self.H % 128 == 0 and self.I % 64 == 0 and 2 * T * self.k >= self.E * m
-                and T * self.k <= 65535)
+                and T * self.k <= 65535 and not self.experts.missing_exp)
 
     def buffers(self, T: int) -> _Buffers:
         b = self._bufs.get(T)
@@ -79,7 +79,7 @@ class MoELayer:
                                     device=x.device)
             D.moe_decode(ex.table, self.E, self.H, self.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, b.row_exp, b.routing,
                          b.y, b.ws, max_rows=self.gemm_min_rows - 1, status=b.status)
-            D.moe_prefill(ex.table, ex.wexp, self.E, self.H, self.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, b.row_exp,
+            D.moe_prefill(ex.table, ex.eexp, self.E, self.H, self.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, b.row_exp,
                           b.routing, b.y, b.pws, min_rows=self.gemm_min_rows, status=b.status)
         else:
             D.moe_decode(ex.table, self.E, self.H, self.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, b.row_exp, b.routing,

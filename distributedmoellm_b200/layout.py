@@ -162,6 +162,41 @@ def weight_exponent(s, qmax: int) -> int:
     return int(min(120, max(-120, 14 - int(ex))))
 
 
+def row_l1_q4(raw: np.ndarray, s, gs: int, offset: bool = False) -> np.ndarray:
+    """Per row sum of |weight| of a colibri int4 matrix (float64)."""
+    raw = np.asarray(raw, np.uint8)
+    O, K = raw.shape[0], raw.shape[1] * 2
+    lo, hi = (raw & 15).astype(np.int16), (raw >> 4).astype(np.int16)
+    if offset:
+        lo, hi = lo - 8, hi - 8
+    else:
+        lo, hi = np.where(lo >= 8, lo - 16, lo), np.where(hi >= 8, hi - 16, hi)
+    g = (np.abs(lo) + np.abs(hi)).reshape(O, K // gs, gs // 2).sum(axis=2)
+    return (g * np.asarray(s, np.float64)).sum(axis=1)
+
+
+def row_l1_q8(q: np.ndarray, s, gs: int) -> np.ndarray:
+    """Per row sum of |weight| of a group-scaled int8 matrix (float64)."""
+    q = np.asarray(q, np.int8)
+    O, K = q.shape
+    g = np.abs(q.astype(np.int16)).reshape(O, K // gs, gs).sum(axis=2)
+    return (g * np.asarray(s, np.float64)).sum(axis=1)
+
+
+def act_exponent(gu_row_l1: np.ndarray, inter: int) -> int:
+    """The activation exponent base a of an expert for the tensor-core path:
+    with a token row's largest value below 2^(14 - row_exp), its SwiGLU
+    activations satisfy |SiLU(g) u| <= |g| |u| < 2^(28 - 2 row_exp) * L1g * L1u
+    (L1g, L1u: the largest row sums of |weight| of the gate and up halves), so
+    scaling them by 2^(a + 2 row_exp) with a = -13 - ceil(log2(L1g * L1u))
+    keeps them below 2^15, inside f16."""
+    l1 = np.asarray(gu_row_l1, np.float64)
+    b = float(l1[:inter].max(initial=0.0)) * float(l1[inter:].max(initial=0.0))
+    if not (0.0 < b < 1e300):
+        return 0
+    return int(min(120, max(-120, -13 - int(np.ceil(np.log2(b))))))
+
+
 def q4_0_as_q4(raw: np.ndarray, cols: int):
     """GGUF Q4_0 rows (O, cols/32 * 18) -> (colibri-order offset nibbles (O,
     cols/2), f16 scales (O, cols/32)).  Q4_0 keeps a block's first 16 values

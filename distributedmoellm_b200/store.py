@@ -38,10 +38,13 @@ class LayerExperts:
         self.buf = torch.zeros(max(1, len(self.ids)) * self.slot_bytes, dtype=torch.uint8, device=self.device)
         self._table_host = np.zeros((E, 2), np.int64)
         self.table = torch.zeros((E, 2), dtype=torch.int64, device=self.device)
-        # per expert, per matrix (gate|up, down): the power-of-two exponent the
-        # tensor-core path scales the weights by before rounding them to f16
-        self._wexp_host = np.zeros((E, 2), np.int32)
-        self.wexp = torch.zeros((E, 2), dtype=torch.int32, device=self.device)
+        # per expert, the power-of-two exponents of the tensor-core path: the
+        # gate|up and down weight exponents (layout.weight_exponent) and the
+        # activation exponent base (layout.act_exponent); experts stored from
+        # raw tiles without them keep the layer on the decode kernels
+        self._eexp_host = np.zeros((E, 4), np.int32)
+        self.eexp = torch.zeros((E, 4), dtype=torch.int32, device=self.device)
+        self.missing_exp: set[int] = set()
         self.present: set[int] = set()
 
     # ---- placement
@@ -50,9 +53,10 @@ class LayerExperts:
         base = i * self.slot_bytes
         return base, base + _al(self.gu_nbytes)
 
-    def put_tiles(self, e: int, gu_tiles, dn_tiles, wexp=(0, 0)) -> None:
+    def put_tiles(self, e: int, gu_tiles, dn_tiles, eexp=None) -> None:
         """Store expert ``e`` from tile bytes (numpy on the host, or uint8 tensors).
-        ``wexp``: the matrices' weight exponents (``layout.weight_exponent``)."""
+        ``eexp``: (gate|up weight exponent, down weight exponent, activation
+        exponent base), needed by the tensor-core path."""
         if e not in self.slot_of:
             raise KeyError(f"expert {e} is not placed on this device")
         g0, d0 = self._slot(e)
@@ -63,24 +67,31 @@ class LayerExperts:
             self.buf[off:off + n].copy_(src.reshape(-1), non_blocking=False)
         base = self.buf.data_ptr()
         self._table_host[e] = (base + g0, base + d0)
-        self._wexp_host[e] = wexp
+        if eexp is None:
+            self._eexp_host[e] = 0
+            self.missing_exp.add(e)
+        else:
+            self._eexp_host[e, :3] = eexp
+            self.missing_exp.discard(e)
         self.present.add(e)
 
     def put_int4(self, e: int, gu_raw, gu_s, dn_raw, dn_s, offset: bool = False) -> None:
         """Expert ``e`` from colibri int4 arrays (moelan Packed4: raw, s)."""
         self.put_tiles(e, layout.q4_tiles(gu_raw, gu_s, self.gs, offset, gu_inter=self.I),
                        layout.q4_tiles(dn_raw, dn_s, self.gs, offset),
-                       (layout.weight_exponent(gu_s, 8), layout.weight_exponent(dn_s, 8)))
+                       (layout.weight_exponent(gu_s, 8), layout.weight_exponent(dn_s, 8),
+                        layout.act_exponent(layout.row_l1_q4(gu_raw, gu_s, self.gs, offset), self.I)))
 
     def put_int8(self, e: int, gu_q, gu_s, dn_q, dn_s) -> None:
         """Expert ``e`` from group-scaled int8 arrays (moelan GroupQuant: q, s)."""
         self.put_tiles(e, layout.q8_tiles(gu_q, gu_s, self.gs, gu_inter=self.I), layout.q8_tiles(dn_q, dn_s, self.gs),
-                       (layout.weight_exponent(gu_s, 128), layout.weight_exponent(dn_s, 128)))
+                       (layout.weight_exponent(gu_s, 128), layout.weight_exponent(dn_s, 128),
+                        layout.act_exponent(layout.row_l1_q8(gu_q, gu_s, self.gs), self.I)))
 
     def publish(self) -> None:
         """Upload the address table after a batch of puts."""
         self.table.copy_(torch.from_numpy(self._table_host))
-        self.wexp.copy_(torch.from_numpy(self._wexp_host))
+        self.eexp.copy_(torch.from_numpy(self._eexp_host))
 
     @property
     def nbytes(self) -> int:

@@ -172,13 +172,17 @@ int64_t mb_moe_prefill_workspace_bytes(int64_t P, int H, int I);
  * ExpertStore.compute (experts.py:707-727) as gate|up, SiLU(gate) * up,
  * down.  Same tables, routing, row_exp and y (P, H) as mb_moe_decode;
  * experts with fewer than min_rows picks are left to mb_moe_decode
- * (max_rows = min_rows - 1).  w_exp (E, 2) int32 (may be NULL = 0): per
- * expert, the power-of-two exponents that bring the largest weight of its
- * gate|up and down matrices into [2^13, 2^14) before rounding to f16.
- * Results agree with the f32 reference within 2e-3 of each output row's
- * largest magnitude.  Needs H % 128 == 0, I % 64 == 0, P <= 65535, x and
- * workspace 16-byte aligned. */
-int mb_moe_prefill(const MbExpert *table, const int32_t *w_exp, int E, int H, int I, int gs, int fmt_gu,
+ * (max_rows = min_rows - 1).  e_exp (E, 4) int32, per expert: the
+ * power-of-two exponents that bring the largest possible weight of its
+ * gate|up and of its down matrix into [2^13, 2^14) before rounding to f16,
+ * then the activation exponent base a: a pick's SwiGLU activations are
+ * scaled by 2^(a + 2 row_exp) before rounding to f16, and a must keep them
+ * below 2^15 (a = -13 - ceil(log2(L1g * L1u)) with L1g, L1u the largest
+ * row sums of |weight| of the gate and up halves does); the fourth entry is
+ * unused.  Results agree with the f32 reference within 2e-3 of each output
+ * row's largest magnitude.  Needs H % 128 == 0, I % 64 == 0, P <= 65535, x
+ * and workspace 16-byte aligned. */
+int mb_moe_prefill(const MbExpert *table, const int32_t *e_exp, int E, int H, int I, int gs, int fmt_gu,
                    int fmt_down, const float *x, const int32_t *row_exp, int64_t T, const int32_t *counts,
                    const int32_t *offsets, const int32_t *sorted_rows, int64_t P, int min_rows, float *y,
                    void *workspace, int64_t workspace_bytes, unsigned *status, void *stream);

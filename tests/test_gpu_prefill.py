@@ -77,7 +77,7 @@ def _run(D, ex, desc, counts, min_rows, seed):
     ws = torch.empty(D.prefill_workspace_bytes(T, H, I), dtype=torch.uint8, device="cuda")
     st = torch.zeros(1, dtype=torch.int32, device="cuda")
     xd = cu(x)
-    D.moe_prefill(ex.table, ex.wexp, E, H, I, ex.gs, ex.fmt_gu, ex.fmt_down, xd, D.row_exponents(xd), r, y, ws,
+    D.moe_prefill(ex.table, ex.eexp, E, H, I, ex.gs, ex.fmt_gu, ex.fmt_down, xd, D.row_exponents(xd), r, y, ws,
                   min_rows=min_rows, status=st)
     torch.cuda.synchronize()
     assert int(st.item()) == 0
@@ -127,7 +127,7 @@ def test_prefill_bad_shape_raises(D):
     ws = torch.empty(D.prefill_workspace_bytes(4, 256, 96), dtype=torch.uint8, device="cuda")
     with pytest.raises(RuntimeError, match="mb_moe_prefill"):
         xd = torch.zeros((4, 256), device="cuda")
-        D.moe_prefill(ex.table, ex.wexp, 2, 256, 96, 32, ex.fmt_gu, ex.fmt_down, xd, D.row_exponents(xd), r, y, ws)
+        D.moe_prefill(ex.table, ex.eexp, 2, 256, 96, 32, ex.fmt_gu, ex.fmt_down, xd, D.row_exponents(xd), r, y, ws)
 
 
 @pytest.fixture(scope="module")
