@@ -4,8 +4,11 @@ One step = one MoE layer of the Qwen3-30B-A3B shape (config 2 of the
 benchmark: d_model 2048, 128 experts, top-8, expert intermediate 768, int4
 group-32 experts with f16 scales) over a decode batch of T tokens: router
 logits -> softmax top-k -> permute by expert -> fused gate|up/SiLU/down
-mat-vecs over the packed experts -> weighted combine.  Synthetic seeded
-inputs (numpy PCG64) with the benchmark's shapes and distributions.
+mat-vecs over the packed experts -> weighted combine.  The line's "prefill"
+object times the same layer at 2048 / 4096 tokens (config 3: int8 group-32
+experts with f32 scales; and the int4 layer), where the experts run as
+grouped GEMMs on the tensor cores.  Synthetic seeded inputs (numpy PCG64)
+with the benchmark's shapes and distributions.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl reference]
 
@@ -50,7 +53,10 @@ def parse():
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--profile", action="store_true",
-                   help="only the main timed loop (for ncu): no e2e, sweep or CPU baseline")
+                   help="only the main timed loop (for ncu): no e2e, sweep, prefill or CPU baseline")
+    p.add_argument("--profile-prefill", action="store_true",
+                   help="only a few prefill steps of the int4 layer at 2048 tokens (for ncu)")
+    p.add_argument("--no-prefill", action="store_true")
     return p.parse_args()
 
 
@@ -67,6 +73,55 @@ def make_experts(seed=0):
     experts = {e: S.int4_expert(rng, H, I, GS, f16_scales=True) for e in range(E)}
     router = S.router(rng, E, H)
     return experts, router
+
+
+def int8_layer(router, dev, seed=3):
+    """Config 3: the same layer with int8 group-32 experts and f32 scales (5.3 MB each, 680 MB)."""
+    import torch
+    from distributedmoellm_b200 import layout as L
+    from distributedmoellm_b200 import synthetic as S
+    from distributedmoellm_b200.layer import MoELayer
+    from distributedmoellm_b200.store import LayerExperts
+    rng = np.random.default_rng(seed)
+    ex = LayerExperts(E, H, I, GS, L.FMT_Q8_F32, L.FMT_Q8_F32, dev)
+    for e in range(E):
+        ex.put_int8(e, *S.int8_expert(rng, H, I, GS))
+    ex.publish()
+    return MoELayer(torch.from_numpy(router).to(dev), ex, K_TOP, True)
+
+
+PREFILL_FLOPS_PER_TOKEN = 2 * K_TOP * 3 * H * I      # 75.5 MFLOP
+
+
+def measure_prefill(layer, T, steps, warmup, world, dev, seed=5):
+    """Graph replays of the whole layer and of its expert kernels alone at T
+    tokens (weights > L2, so every step streams them from HBM)."""
+    import torch
+    import torch.distributed as dist
+    x = torch.from_numpy(np.random.default_rng(seed).standard_normal((T, H), dtype=np.float32)).to(dev)
+    full = layer.capture(x)
+    ex = layer.capture(x, experts_only=True)
+    torch.cuda.synchronize()
+
+    def timed(g, n):
+        for _ in range(warmup):
+            g.replay()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / n
+
+    ms, ex_ms = timed(full, steps), timed(ex, steps)
+    st = int(layer.status(T))
+    gemm = layer.uses_gemm(T)
+    del full, ex
+    return ms, ex_ms, st, gemm
 
 
 # ---- clocks sampled during the timed region ------------------------------------------
@@ -217,10 +272,13 @@ def run_gpu(args, rank, world, dev):
     T = args.tokens
     gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(dev.index or 0)).split(",")[dev.index or 0]) \
         if os.environ.get("CUDA_VISIBLE_DEVICES", "").replace(",", "").isdigit() else (dev.index or 0)
+    if args.profile_prefill:
+        ms, ex_ms, status, _ = measure_prefill(layers[0], 2048, args.steps, args.warmup, world, dev)
+        return world * 2048 / (ms / 1e3), ms, {}, {}, {}, None, {}, status, {}
     with Clocks(gpu_index) as clk:
         ms, dec_ms, u_avg, status = measure(T, args.steps, args.warmup)
     if args.profile:
-        return world * T / (ms / 1e3), ms, {}, {}, {}, None, clk.summary(), status
+        return world * T / (ms / 1e3), ms, {}, {}, {}, None, clk.summary(), status, {}
     ms = max_over_ranks(ms)
     value = world * T / (ms / 1e3)
 
@@ -249,6 +307,24 @@ def run_gpu(args, rank, world, dev):
                                       "unique_experts": u}
             status = max(status, st)
 
+    prefill = {}
+    if not args.no_prefill:
+        l8 = int8_layer(router, dev)
+        tf_peak = pk.get("bf16_tflops", 1590.0)
+        for name, layer, Tp in (("int8_T2048", l8, 2048), ("int8_T4096", l8, 4096), ("int4_T2048", layers[0], 2048)):
+            m, em, st, gemm = measure_prefill(layer, Tp, max(10, args.steps // 8), 3, world, dev)
+            m, em = max_over_ranks(m), max_over_ranks(em)
+            fl = Tp * PREFILL_FLOPS_PER_TOKEN
+            prefill[name] = {"tokens_per_s": round(world * Tp / (m / 1e3), 1), "ms_per_step": round(m, 5),
+                             "experts_ms": round(em, 5), "grouped_gemm": gemm,
+                             "roofline": {"bound": "tensor", "achieved": round(fl / (em / 1e3) / 1e12, 1),
+                                          "peak": tf_peak, "unit": "TFLOP/s",
+                                          "frac": round(fl / (em / 1e3) / 1e12 / tf_peak, 4),
+                                          "peak_kind": pk_kind + " bf16 dense (f16 runs at the same rate)",
+                                          "kernel": "expert kernels (gather + gate|up GEMM + down GEMM)"}}
+            status = max(status, st)
+        del l8
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         step, O = cpu_step_fn(experts, router, T)
@@ -256,7 +332,7 @@ def run_gpu(args, rank, world, dev):
         cpu = {"value": round(T / s_per, 2), "unit": UNIT, "cores": O.threads(), "kind": "port",
                "sample": f"{n} MoE-layer steps of T={T} tokens (all 128 experts resident in host RAM), "
                          f"C+OpenMP restatement of moelan's fused int4 layer kernel + numpy routing"}
-    return value, ms, roof, e2e, sweep, cpu, clk.summary(), status
+    return value, ms, roof, e2e, sweep, cpu, clk.summary(), status, prefill
 
 
 def measure_e2e(layers, T, steps, warmup, world, dev):
@@ -341,14 +417,16 @@ def main():
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    value, ms, roof, e2e, sweep, cpu, clocks, status = run_gpu(args, rank, world, dev)
+    value, ms, roof, e2e, sweep, cpu, clocks, status, prefill = run_gpu(args, rank, world, dev)
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "f32 activations x int4 weights (f16 tensor-core pieces, f32 accum)",
+                "vs_baseline": None, "dtype": "f32",
+                "dtype_note": "decode: int4 weights x f32 activations, products exact (f16 pieces), f32 sums; "
+                              "prefill: f16 tensor-core operands with power-of-two range scaling, f32 sums",
                 "data": "synthetic", "config": workload_config(args), "roofline": roof, "cpu_baseline": cpu,
                 "e2e": e2e, "clocks": clocks, "gpu_launches": 6 * args.steps, "sweep": sweep,
-                "kernel_status": status}
+                "prefill": prefill, "kernel_status": status}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
