@@ -49,7 +49,8 @@ constexpr int kBM = 128;       // weight rows per item = TMEM lanes
 // 128-byte swizzle atom of f16), the unit of every hand-off.
 constexpr int kMaxN = 192;     // tokens per pass
 constexpr int kBStages = 3;    // token (B) quad stages: [2 halves][kMaxN rows][128 B] = 48 KB each
-constexpr int kPStages = 4;    // packed-weight stages, one quad of 8 row tiles each
+constexpr int pstages(bool q8) { return q8 ? 3 : 4; }   // packed-weight stages, one quad of 8 row tiles each
+constexpr int kMaxMetaE = 512; // experts whose (count, offset, exponents) a CTA keeps in shared memory
 constexpr int kASlots = 2;     // A (dequantised quad) slots in TMEM, 64 columns each, one per dequant set
 constexpr int kAccCol = kASlots * 64;
 constexpr int kTmemCols = 512;
@@ -212,11 +213,14 @@ __device__ __forceinline__ int clamp120(int e) { return e < -120 ? -120 : (e > 1
 // The static sequence of work items every role of a CTA walks: items
 // blockIdx.x, blockIdx.x + gridDim.x, ... of E * MB, skipping experts
 // outside this launch.
+// meta[e] = (picks, first pick, this launch's weight exponent, activation exponent base), staged in
+// shared memory once per CTA.
 struct Items {
     const PrefillArgs& a;
+    const int4* meta;
     int it;
-    int e, mb, n_e, off_e, passes;
-    __device__ explicit Items(const PrefillArgs& args) : a(args), it((int)blockIdx.x - (int)gridDim.x) {}
+    int e, mb, n_e, off_e, passes, wexp, aexp;
+    __device__ Items(const PrefillArgs& args, const int4* m) : a(args), meta(m), it((int)blockIdx.x - (int)gridDim.x) {}
     __device__ bool next()
     {
         for (;;) {
@@ -224,15 +228,29 @@ struct Items {
             if (it >= a.E * a.MB) return false;
             e = it / a.MB;
             mb = it - e * a.MB;
-            n_e = a.counts[e];
+            const int4 m = meta[e];
+            n_e = m.x;
             if (n_e >= a.min_rows && n_e > 0) {
-                off_e = a.offsets[e];
+                off_e = m.y;
+                wexp = m.z;
+                aexp = m.w;
                 passes = (n_e + kMaxN - 1) / kMaxN;
                 return true;
             }
         }
     }
 };
+
+// v[t] = the loaded v[(t - rot) & 3]: undoes a load order rotated by rot.
+__device__ __forceinline__ void rotate_back(uint4 (&v)[4], int rot)
+{
+    const bool r1 = rot & 1, r2 = rot & 2;
+    uint4 u[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) u[t] = r1 ? v[(t + 3) & 3] : v[t];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) v[t] = r2 ? u[(t + 2) & 3] : u[t];
+}
 
 // ---- the GEMM kernel ----------------------------------------------------------------
 
@@ -243,6 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr bool Q8 = (FMT == MB_FMT_Q8_F16 || FMT == MB_FMT_Q8_F32);
     constexpr bool F16S = (FMT == MB_FMT_Q4_F16 || FMT == MB_FMT_Q8_F16);
     constexpr int kData = Q8 ? 2048 : 1024;
+    constexpr int kPStages = pstages(Q8);
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -261,8 +280,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* acc_empty = acc_full + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int4* meta = reinterpret_cast<int4*>(tmem_slot + 4);       // [E]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int e = threadIdx.x; e < a.E; e += kThreads) {
+        const int* ee = a.e_exp + 4 * e;
+        meta[e] = make_int4(a.counts[e], a.offsets[e], ee[a.phase == 1 ? 0 : 1], ee[2]);
+    }
     if (threadIdx.x == 0) {
         for (int i = 0; i < kBStages; ++i) {
             mb_mbar_init(&b_full[i], 1);
@@ -296,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ------------------------------------------------------------ weight producer
         if (lane == 0) {
-            Items w(a);
+            Items w(a, meta);
             int64_t gq = 0;
             while (w.next() && !*abort_flag) {
                 const int tiles = min(8, a.RT - w.mb * 8);
@@ -321,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------ token producer
         if (lane == 0) {
-            Items w(a);
+            Items w(a, meta);
             int64_t gq = 0;
             while (w.next() && !*abort_flag) {
                 for (int pass = 0; pass < w.passes; ++pass) {
@@ -346,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 2) {
         // ------------------------------------------------------------ MMA issuer (whole warp, one lane issues)
-        Items w(a);
+        Items w(a, meta);
         int64_t gq = 0;
         int64_t np = 0;   // passes issued (accumulator buffer np & 1)
         bool ok = true;
@@ -397,13 +421,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             trow = L & 15;
         }
         const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + set * 64;
-        Items w(a);
+        Items w(a, meta);
         int64_t gq = 0;
         while (w.next()) {
             const int tiles = min(8, a.RT - w.mb * 8);
             const bool row_ok = ti < tiles;
-            const int wexp = a.e_exp[4 * w.e + (a.phase == 1 ? 0 : 1)];
-            const float wscale = pow2i(clamp120(wexp));
+            const float wscale = pow2i(clamp120(w.wexp));
             for (int pass = 0; pass < w.passes; ++pass) {
                 for (int qd = 0; qd < quads; ++qd, ++gq) {
                     if ((int)(gq & 1) != set) continue;
@@ -435,6 +458,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!ok || !row_ok) s2[0] = s2[1] = s2[2] = s2[3] = 0u;
                     // half hh covers groups 2hh, 2hh+1; TMEM column 32*hh + 16*gl + 4*t + i of the slot holds
                     // the f16 pair (column 8t+i, column 8t+i+4) of group 2hh+gl.
+                    // A row's four 16-byte lane words are read starting at word rot = (trow >> 1) & 3 (so the
+                    // eight rows of a quarter-warp hit eight different bank groups) and rotated back.
+                    const int rot = (trow >> 1) & 3;
+                    uint4 W4[4];
+                    if (!Q8) {
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            W4[k] = *reinterpret_cast<const uint4*>(blk + trow * 64 + ((k + rot) & 3) * 16);
+                        rotate_back(W4, rot);
+                    }
                     for (int hh = 0; hh < nh; ++hh) {
                         uint32_t v[32];
                         if (!Q8) {
@@ -442,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             // u = v + 8) of each of the quad's four groups.
 #pragma unroll
                             for (int t = 0; t < 4; ++t) {
-                                const uint2 wv = *reinterpret_cast<const uint2*>(blk + trow * 64 + t * 16 + 8 * hh);
+                                const uint2 wv = hh ? make_uint2(W4[t].z, W4[t].w) : make_uint2(W4[t].x, W4[t].y);
 #pragma unroll
                                 for (int gl = 0; gl < 2; ++gl) {
                                     const uint32_t wd = gl ? wv.y : wv.x, w8 = wd >> 8;
@@ -465,8 +498,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                             // each (group 2hh + gl at byte 8 gl), bytes u = q + 128 in the order
                             // c0 c4 c1 c5 c2 c6 c3 c7: byte pair i is the pair (8t+i, 8t+i+4).
 #pragma unroll
+                            for (int k = 0; k < 4; ++k)
+                                W4[k] = *reinterpret_cast<const uint4*>(blk + hh * 1024 + trow * 64 + ((k + rot) & 3) * 16);
+                            rotate_back(W4, rot);
+#pragma unroll
                             for (int t = 0; t < 4; ++t) {
-                                const uint4 wv = *reinterpret_cast<const uint4*>(blk + hh * 1024 + trow * 64 + t * 16);
+                                const uint4 wv = W4[t];
 #pragma unroll
                                 for (int gl = 0; gl < 2; ++gl) {
                                     const uint32_t w0 = gl ? wv.z : wv.x, w1 = gl ? wv.w : wv.y;
@@ -497,12 +534,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int L = 32 * q + lane;
         const int et = threadIdx.x - 32 * (4 + kDqWarps);   // 0..127
         const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
-        Items w(a);
+        Items w(a, meta);
         int64_t np = 0;
         while (w.next()) {
-            const int* ee = a.e_exp + 4 * w.e;
-            const int wexp = ee[a.phase == 1 ? 0 : 1];
-            const float wunscale = pow2i(-clamp120(wexp));
+            const float wunscale = pow2i(-clamp120(w.wexp));
             for (int pass = 0; pass < w.passes; ++pass, ++np) {
                 const int slot = (int)(np & 1);
                 const int n0 = pass * kMaxN;
@@ -514,7 +549,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     float s0 = 0.f, s1 = 0.f;
                     if (n < nrows) {
                         const int rexp = a.row_exp[a.sorted_rows[w.off_e + n0 + n]];
-                        const int ea = clamp120(ee[2] + 2 * rexp);
+                        const int ea = clamp120(w.aexp + 2 * rexp);
                         s0 = pow2i(a.phase == 1 ? -clamp120(rexp) : -ea);
                         s1 = pow2i(ea);
                     }
@@ -648,17 +683,18 @@ int block_bytes_of(int fmt)
     return (q8 ? 2048 : 1024) + 64 * (f16 ? 2 : 4);
 }
 
-size_t smem_bytes(int block_bytes)
+size_t smem_bytes(int fmt, int block_bytes, int E)
 {
-    return 1024 + (size_t)kBStages * 2 * kBHalf + (size_t)kPStages * 8 * block_bytes + 4 * kMaxN * 4 +
-           (2 * kBStages + 2 * kPStages + 2 * kASlots + 4) * 8 + 64;
+    const int ps = pstages(fmt == MB_FMT_Q8_F16 || fmt == MB_FMT_Q8_F32);
+    return 1024 + (size_t)kBStages * 2 * kBHalf + (size_t)ps * 8 * block_bytes + 4 * kMaxN * 4 +
+           (2 * kBStages + 2 * ps + 2 * kASlots + 4) * 8 + 16 + (size_t)E * 16;
 }
 
 template <int FMT>
 int launch(const PrefillArgs& a, const CUtensorMap& map, cudaStream_t st)
 {
     auto kern = prefill_kernel<FMT>;
-    const size_t smem = smem_bytes(a.block_bytes);
+    const size_t smem = smem_bytes(FMT, a.block_bytes, a.E);
     static thread_local size_t set[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -702,7 +738,8 @@ extern "C" int mb_moe_prefill(const MbExpert* table, const int32_t* e_exp, int E
 {
     MB_REQUIRE(table && e_exp && x && row_exp && counts && offsets && sorted_rows && y && workspace,
                "mb_moe_prefill: null pointer");
-    MB_REQUIRE(E > 0 && E <= 65535 && T >= 0 && P >= 0, "mb_moe_prefill: bad sizes");
+    MB_REQUIRE(E > 0 && E <= kMaxMetaE && T >= 0 && P >= 0, "mb_moe_prefill: E=%d (at most %d experts)", E,
+               kMaxMetaE);
     MB_REQUIRE(H % 128 == 0 && I % 64 == 0 && H > 0 && I > 0,
                "mb_moe_prefill: needs H %% 128 == 0 and I %% 64 == 0 (H=%d I=%d)", H, I);
     MB_REQUIRE(gs % 32 == 0 && H % gs == 0 && I % gs == 0, "mb_moe_prefill: group size %d", gs);
