@@ -47,11 +47,15 @@ namespace {
 constexpr int kBM = 128;       // weight rows per item = TMEM lanes
 // The K loop runs in quads of 128 columns (two 64-column halves, each one
 // 128-byte swizzle atom of f16), the unit of every hand-off.
-constexpr int kMaxN = 192;     // tokens per pass
-constexpr int kBStages = 3;    // token (B) quad stages: [2 halves][kMaxN rows][128 B] = 48 KB each
-constexpr int pstages(bool q8) { return q8 ? 3 : 4; }   // packed-weight stages, one quad of 8 row tiles each
+constexpr int kMaxN = 160;     // tokens per pass
+constexpr int kBStages = 3;    // token (B) quad stages: [2 halves][kMaxN rows][128 B] = 40 KB each
+// Packed-weight stages, one quad of 8 row tiles each.  Even, so that every stage is always consumed by the
+// same dequant set (sets alternate quads): a set then waits on a stage's next phase only after it consumed
+// the previous one, which keeps the mbarrier parity waits unambiguous.
+constexpr int pstages(bool) { return 4; }
+static_assert(pstages(false) % 2 == 0 && pstages(true) % 2 == 0, "weight stages must be even");
 constexpr int kMaxMetaE = 512; // experts whose (count, offset, exponents) a CTA keeps in shared memory
-constexpr int kASlots = 2;     // A (dequantised quad) slots in TMEM, 64 columns each, one per dequant set
+constexpr int kASlots = 3;     // A (dequantised quad) slots in TMEM, 64 columns each: quad gq uses slot gq % 3
 constexpr int kAccCol = kASlots * 64;
 constexpr int kTmemCols = 512;
 static_assert(kAccCol + 2 * kMaxN <= kTmemCols, "TMEM columns");
@@ -59,6 +63,8 @@ constexpr int kDqWarps = 8;    // warps 4..11: two sets of four (one per TMEM la
 constexpr int kEpiWarps = 4;   // warps 12..15
 constexpr int kThreads = 512;
 constexpr int kBHalf = kMaxN * 128;   // bytes of one half (64 columns) of a token stage
+constexpr int kBoxRows = 32;          // token rows per TMA box (kMaxN is a multiple, so boxes never overrun)
+static_assert(kMaxN % kBoxRows == 0 && kBHalf % 1024 == 0, "token stage layout");
 
 struct PrefillArgs {
     const MbExpert* table;
@@ -315,13 +321,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int KH = a.KH;
     const int quads = (KH + 1) >> 1;   // quads per pass; the last one has one half when KH is odd
 
-    // Every role counts quads gq over all its items and passes: weight stage gq % kPStages, A slot gq % 2
-    // (dequant set gq % 2), token stage gq % kBStages.
+    // Every role counts quads gq over all its items and passes: weight stage gq % kPStages, A slot
+    // gq % kASlots, token stage gq % kBStages, dequant set gq % 2.
     if (warp == 0) {
         // ------------------------------------------------------------ weight producer
         if (lane == 0) {
             Items w(a, meta);
-            int64_t gq = 0;
+            int gq = 0;
             while (w.next() && !*abort_flag) {
                 const int tiles = min(8, a.RT - w.mb * 8);
                 const uint8_t* wbase =
@@ -346,12 +352,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------ token producer
         if (lane == 0) {
             Items w(a, meta);
-            int64_t gq = 0;
+            int gq = 0;
             while (w.next() && !*abort_flag) {
                 for (int pass = 0; pass < w.passes; ++pass) {
                     const int n0 = pass * kMaxN;
                     const int nrows = min(kMaxN, w.n_e - n0);
-                    const int nbox = (((nrows + 15) & ~15) + 63) / 64;
+                    const int nbox = (((nrows + 15) & ~15) + kBoxRows - 1) / kBoxRows;   // <= kMaxN / kBoxRows
                     for (int qd = 0; qd < quads; ++qd, ++gq) {
                         const int bs = (int)(gq % kBStages);
                         const int nh = min(2, KH - 2 * qd);
@@ -359,11 +365,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                             !mb_mbar_wait_spin(&b_empty[bs], (uint32_t)(((gq / kBStages) - 1) & 1), a.status,
                                                abort_flag))
                             break;
-                        mb_mbar_arrive_expect_tx(&b_full[bs], (uint32_t)(nh * nbox * 64 * 128));
+                        mb_mbar_arrive_expect_tx(&b_full[bs], (uint32_t)(nh * nbox * kBoxRows * 128));
                         for (int hh = 0; hh < nh; ++hh)
                             for (int i = 0; i < nbox; ++i)
-                                tma_load_2d(bst + ((size_t)(bs * 2 + hh) * kMaxN + i * 64) * 128, &bmap,
-                                            qd * 128 + hh * 64, w.off_e + n0 + i * 64, &b_full[bs]);
+                                tma_load_2d(bst + ((size_t)(bs * 2 + hh) * kMaxN + i * kBoxRows) * 128, &bmap,
+                                            qd * 128 + hh * 64, w.off_e + n0 + i * kBoxRows, &b_full[bs]);
                     }
                 }
             }
@@ -371,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 2) {
         // ------------------------------------------------------------ MMA issuer (whole warp, one lane issues)
         Items w(a, meta);
-        int64_t gq = 0;
+        int gq = 0;
         int64_t np = 0;   // passes issued (accumulator buffer np & 1)
         bool ok = true;
         while (ok && w.next()) {
@@ -385,10 +391,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 const uint32_t dcol = tmem + kAccCol + slot * kMaxN;
                 for (int qd = 0; ok && qd < quads; ++qd, ++gq) {
-                    const int as = (int)(gq & 1), bs = (int)(gq % kBStages);
+                    const int as = gq % kASlots, bs = gq % kBStages;
                     const int nh = min(2, KH - 2 * qd);
                     ok = __all_sync(0xffffffffu,
-                                    mb_mbar_wait_spin(&a_full[as], (uint32_t)((gq >> 1) & 1), a.status, abort_flag) &&
+                                    mb_mbar_wait_spin(&a_full[as], (uint32_t)((gq / kASlots) & 1), a.status, abort_flag) &&
                                         mb_mbar_wait_spin(&b_full[bs], (uint32_t)((gq / kBStages) & 1), a.status,
                                                           abort_flag));
                     if (!ok) break;
@@ -420,9 +426,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             ti = L >> 4;
             trow = L & 15;
         }
-        const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + set * 64;
+        const uint32_t taddr0 = tmem + ((uint32_t)(32 * q) << 16);
         Items w(a, meta);
-        int64_t gq = 0;
+        int gq = 0;
         while (w.next()) {
             const int tiles = min(8, a.RT - w.mb * 8);
             const bool row_ok = ti < tiles;
@@ -432,10 +438,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if ((int)(gq & 1) != set) continue;
                     const int ps = (int)(gq % kPStages);
                     const int nh = min(2, KH - 2 * qd);
-                    const int64_t use = gq >> 1;     // uses of this set's A slot so far
+                    const int as = gq % kASlots, use = gq / kASlots;   // A slot and its uses so far
+                    const uint32_t taddr = taddr0 + as * 64;
                     bool ok = mb_mbar_wait_spin(&p_full[ps], (uint32_t)((gq / kPStages) & 1), a.status, abort_flag);
                     if (use >= 1)
-                        ok = mb_mbar_wait_spin(&a_empty[set], (uint32_t)((use - 1) & 1), a.status, abort_flag) && ok;
+                        ok = mb_mbar_wait_spin(&a_empty[as], (uint32_t)((use - 1) & 1), a.status, abort_flag) && ok;
                     tc_fence_after();
                     const uint8_t* blk = pst + ((size_t)ps * 8 + (row_ok ? ti : 0)) * a.block_bytes;
                     // the quad's four group scales, times 2^wexp, as f16x2 pairs (s, s)
@@ -522,7 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) {
-                        mb_mbar_arrive(&a_full[set]);
+                        mb_mbar_arrive(&a_full[as]);
                         mb_mbar_arrive(&p_empty[ps]);
                     }
                 }
@@ -659,7 +666,7 @@ int encode_fn(EncodeTiledFn* out)
     return MB_OK;
 }
 
-// Tensor map of a (rows, cols) row-major f16 matrix, boxes of 64 columns x 64 rows, 128-byte swizzle.
+// Tensor map of a (rows, cols) row-major f16 matrix, boxes of 64 columns x kBoxRows rows, 128-byte swizzle.
 int f16_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols)
 {
     EncodeTiledFn fn;
@@ -667,7 +674,7 @@ int f16_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols)
     if (rc) return rc;
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    const cuuint32_t box[2] = {64, 64};
+    const cuuint32_t box[2] = {64, kBoxRows};
     const cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
