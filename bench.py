@@ -41,6 +41,10 @@ EXPERT_BYTES = 2 * I * H // 2 + 2 * I * (H // GS) * 2 + H * I // 2 + H * (I // G
 METRIC = "moe_layer_tokens_per_s"
 UNIT = "tokens/s"
 L2_ROTATE_LAYERS = 4
+# DRAM bytes (read + write) of one decode step's two expert-kernel launches at
+# T=64, from one ncu capture of `bench.py --profile` (the dominant kernel's
+# traffic; other token counts report None)
+NCU_DECODE_TRAFFIC = {64: 346_000_000}
 
 
 def parse():
@@ -286,7 +290,7 @@ def run_gpu(args, rank, world, dev):
     alg_bytes = u_avg * EXPERT_BYTES + T * H * 4 + T * K_TOP * H * 4
     achieved = alg_bytes / (dec_ms / 1e3) / 1e9
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-            "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None, "peak_kind": pk_kind,
+            "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": NCU_DECODE_TRAFFIC.get(T), "peak_kind": pk_kind,
             "kernel": "moe_decode_kernel (gate|up + down phases)", "kernel_ms": round(dec_ms, 5),
             "alg_bytes_per_launch": int(alg_bytes), "unique_experts": u_avg}
 

@@ -91,14 +91,38 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int nslices
     const int per = (E + 31) / 32;
     float v[kTopkMaxPerLane];
     float m = -FLT_MAX;
+    if (nslices > 0) {
+        // sum the slices in slice order; four slices' loads per element are in flight at once
+#pragma unroll
+        for (int i = 0; i < kTopkMaxPerLane; ++i) v[i] = 0.f;
+        const int64_t sstride = T * E;
+        for (int sl = 0; sl < nslices; sl += 4) {
+            const int nl = min(4, nslices - sl);
+#pragma unroll
+            for (int i = 0; i < kTopkMaxPerLane; ++i) {
+                const int e = i * 32 + lane;
+                if (i < per && e < E) {
+                    const float* src = logits + ((int64_t)sl * T + t) * E + e;
+                    const float l0 = src[0];
+                    const float l1 = nl > 1 ? src[sstride] : 0.f;
+                    const float l2 = nl > 2 ? src[2 * sstride] : 0.f;
+                    const float l3 = nl > 3 ? src[3 * sstride] : 0.f;
+                    float acc = v[i] + l0;
+                    if (nl > 1) acc += l1;
+                    if (nl > 2) acc += l2;
+                    if (nl > 3) acc += l3;
+                    v[i] = acc;
+                }
+            }
+        }
+    }
 #pragma unroll
     for (int i = 0; i < kTopkMaxPerLane; ++i) {
         const int e = i * 32 + lane;
         float val = -INFINITY;
         if (i < per && e < E) {
             if (nslices > 0) {
-                val = 0.f;
-                for (int sl = 0; sl < nslices; ++sl) val += logits[((int64_t)sl * T + t) * E + e];
+                val = v[i];
                 if (out_logits) out_logits[t * E + e] = val;
             } else {
                 val = logits[t * E + e];
@@ -107,10 +131,11 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int nslices
         }
         v[i] = val;
     }
-    if (row_exp && part_max && lane == 0) {
+    if (row_exp && part_max) {
         float xm = 0.f;
-        for (int sl = 0; sl < nslices; ++sl) xm = fmaxf(xm, part_max[(int64_t)sl * T + t]);
-        row_exp[t] = mb_row_exponent(xm);
+        for (int sl = lane; sl < nslices; sl += 32) xm = fmaxf(xm, part_max[(int64_t)sl * T + t]);
+        for (int o = 16; o; o >>= 1) xm = fmaxf(xm, __shfl_xor_sync(0xffffffffu, xm, o));
+        if (lane == 0) row_exp[t] = mb_row_exponent(xm);
     }
     for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float sum = 0.0f;
