@@ -211,16 +211,112 @@ def build_layers(experts, router, dev, n_layers):
         base.put_int4(e, gr, gsc, dr, dsc, offset=False)
     base.publish()
     rt = torch.from_numpy(router).to(dev)
-    layers = [MoELayer(rt, base, K_TOP, True)]
-    for _ in range(n_layers - 1):          # same bytes at other addresses: each step streams from HBM
-        ex = LayerExperts(E, H, I, GS, L.FMT_Q4_F16, L.FMT_Q4_F16, dev)
+    return [MoELayer(rt, ex, K_TOP, True) for ex in clone_experts(base, n_layers)]
+
+
+def clone_experts(base, n):
+    """n layers of the same expert bytes at different addresses (so that
+    rotating over them streams every step's weights from HBM, not L2)."""
+    from distributedmoellm_b200.store import LayerExperts
+    out = [base]
+    for _ in range(n - 1):
+        ex = LayerExperts(base.E, base.H, base.I, base.gs, base.fmt_gu, base.fmt_down, base.device)
         ex.buf.copy_(base.buf)
         off = ex.buf.data_ptr() - base.buf.data_ptr()
         ex._table_host = base._table_host + np.where(base._table_host != 0, off, 0)
+        ex._eexp_host = base._eexp_host.copy()
         ex.present = set(base.present)
         ex.publish()
-        layers.append(MoELayer(rt, ex, K_TOP, True))
-    return layers
+        out.append(ex)
+    return out
+
+
+def run_gpu_ep(args, rank, world, dev):
+    """Expert parallelism over the world's GPUs: rank r holds experts
+    r*E/N .. (r+1)*E/N - 1 and T tokens of its own; picked rows go to their
+    experts' ranks and back by NCCL all-to-all (distributedmoellm_b200.ep)."""
+    import torch
+    import torch.distributed as dist
+    from distributedmoellm_b200 import device as D
+    from distributedmoellm_b200 import layout as L
+    from distributedmoellm_b200 import synthetic as S
+    from distributedmoellm_b200.ep import DeviceOps, EPLayer
+    from distributedmoellm_b200.store import LayerExperts
+    D.require_device()
+    experts, router = make_experts(0)
+    El = E // world
+    rt = torch.from_numpy(router).to(dev)
+    base = LayerExperts(El, H, I, GS, L.FMT_Q4_F16, L.FMT_Q4_F16, dev)
+    for j in range(El):
+        base.put_int4(j, *experts[rank * El + j])
+    base.publish()
+    layers = [EPLayer(DeviceOps(rt, ex, E, K_TOP), E, K_TOP, H) for ex in clone_experts(base, L2_ROTATE_LAYERS * world)]
+    pk, pk_kind = peaks()
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def measure(lays, T, steps, warmup, seed, host=False):
+        rng = np.random.default_rng(seed + 31 * rank)
+        hx = [torch.from_numpy(rng.standard_normal((T, H), dtype=np.float32)) for _ in lays]
+        if host:
+            hx = [h.pin_memory() for h in hx]
+            hout = torch.empty((T, H), dtype=torch.float32).pin_memory()
+        xs = [h.to(dev) for h in hx]
+        n = len(lays)
+
+        def step(i):
+            if host:
+                xs[i % n].copy_(hx[i % n], non_blocking=True)
+            out = lays[i % n](xs[i % n])
+            if host:
+                hout.copy_(out, non_blocking=True)
+
+        for i in range(warmup):
+            step(i)
+        dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(steps):
+            step(i)
+        b.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        return max_over_ranks(a.elapsed_time(b) / steps)
+
+    T = args.tokens
+    gpu_index = dev.index or 0
+    with Clocks(gpu_index) as clk:
+        ms = measure(layers, T, args.steps, args.warmup, 1000)
+    value = world * T / (ms / 1e3)
+    e_ms = measure(layers, T, max(10, args.steps // 2), 3, 2000, host=True)
+    e2e = {"value": round(world * T / (e_ms / 1e3), 1), "unit": UNIT, "h2d_bytes_per_step": T * H * 4,
+           "d2h_bytes_per_step": T * H * 4,
+           "api": "distributedmoellm_b200.ep.EPLayer (eager: the all-to-all sizes come from the host)"}
+    # whole-step HBM fraction of one rank: its local expert bytes streamed per step over the step time
+    alg = El * EXPERT_BYTES + T * H * 4 * 2
+    roof = {"bound": "hbm", "achieved": round(alg / (ms / 1e3) / 1e9, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": round(alg / (ms / 1e3) / 1e9 / pk["hbm_gbs"], 4), "traffic": None, "peak_kind": pk_kind,
+            "kernel": "whole EP step per rank (route, exchange, local experts, exchange, combine)",
+            "alg_bytes_per_launch": int(alg)}
+    prefill = {}
+    if not args.no_prefill:
+        rng = np.random.default_rng(3)
+        q8 = LayerExperts(El, H, I, GS, L.FMT_Q8_F32, L.FMT_Q8_F32, dev)
+        for e in range(E):
+            parts = S.int8_expert(rng, H, I, GS)
+            if e // El == rank:
+                q8.put_int8(e - rank * El, *parts)
+        q8.publish()
+        pl = [EPLayer(DeviceOps(rt, q8, E, K_TOP), E, K_TOP, H)]
+        for Tp in (2048,):
+            m = measure(pl, Tp, max(10, args.steps // 8), 3, 3000)
+            prefill[f"int8_T{Tp}_ep{world}"] = {"tokens_per_s": round(world * Tp / (m / 1e3), 1),
+                                               "ms_per_step": round(m, 5)}
+    return value, ms, roof, e2e, {}, None, clk.summary(), 0, prefill
 
 
 def run_gpu(args, rank, world, dev):
@@ -401,7 +497,9 @@ def run_reference(args):
 def workload_config(args):
     return {"workload": f"qwen3-30b-a3b moe layer decode, T={args.tokens} tokens/step per GPU",
             "d_model": H, "experts": E, "top_k": K_TOP, "expert_inter": I, "weights": "int4 g32 f16 scales",
-            "tokens_per_gpu": args.tokens, "parallelism": f"replicas{args.gpus}" if args.gpus > 1 else "single",
+            "tokens_per_gpu": args.tokens,
+            "parallelism": f"ep{args.gpus} (experts {E // args.gpus} per GPU, NCCL all-to-all of routed rows)"
+            if args.gpus > 1 else "single",
             "l2": f"{L2_ROTATE_LAYERS} layers of experts rotated per step (each ~340 MB > 126 MB L2)"}
 
 
@@ -421,7 +519,10 @@ def main():
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    value, ms, roof, e2e, sweep, cpu, clocks, status, prefill = run_gpu(args, rank, world, dev)
+    if world > 1:
+        value, ms, roof, e2e, sweep, cpu, clocks, status, prefill = run_gpu_ep(args, rank, world, dev)
+    else:
+        value, ms, roof, e2e, sweep, cpu, clocks, status, prefill = run_gpu(args, rank, world, dev)
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
@@ -429,7 +530,7 @@ def main():
                 "dtype_note": "decode: int4 weights x f32 activations, products exact (f16 pieces), f32 sums; "
                               "prefill: f16 tensor-core operands with power-of-two range scaling, f32 sums",
                 "data": "synthetic", "config": workload_config(args), "roofline": roof, "cpu_baseline": cpu,
-                "e2e": e2e, "clocks": clocks, "gpu_launches": 6 * args.steps, "sweep": sweep,
+                "e2e": e2e, "clocks": clocks, "gpu_launches": (6 if world == 1 else 9) * args.steps, "sweep": sweep,
                 "prefill": prefill, "kernel_status": status}
         print(json.dumps(line), flush=True)
     if world > 1:

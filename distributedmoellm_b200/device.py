@@ -139,6 +139,17 @@ class Routing:
         self.uoffsets = torch.empty(E + 1, **i32)
         self.n_unique = torch.empty(1, **i32)
 
+    @classmethod
+    def from_plan(cls, counts: torch.Tensor, offsets: torch.Tensor, sorted_rows: torch.Tensor) -> "Routing":
+        """A grouping made elsewhere (expert parallelism: rows received from
+        other ranks): per-expert counts (E,), offsets (E+1,) and the row of
+        each grouped pick (P,), all int32 on the device."""
+        r = cls.__new__(cls)
+        r.E, r.P, r.T, r.k = counts.numel(), sorted_rows.numel(), sorted_rows.numel(), 1
+        r.counts, r.offsets, r.sorted_rows = counts.contiguous(), offsets.contiguous(), sorted_rows.contiguous()
+        r.sorted_w = r.inv = r.uexperts = r.uoffsets = r.n_unique = None
+        return r
+
 
 def permute(idx: torch.Tensor, w: torch.Tensor | None, E: int, r: Routing | None = None) -> Routing:
     _cuda(idx, w)

@@ -1,0 +1,157 @@
+"""Expert parallelism: one MoE layer over G GPUs, one process per GPU.
+
+The reference's own multi-machine design (moelan/coordinator.py:475-535)
+sends each worker one request per layer carrying only the rows routed to its
+experts and adds the partial sums back.  Here the workers are the GPUs of
+one node and the transport is NCCL all-to-all over NVLink:
+
+1. every rank routes its own tokens (the router is replicated) and sorts its
+   picks by expert (mb_router_route, mb_permute);
+2. experts are placed in contiguous slices (expert e on rank e // (E/G)), so
+   the sorted picks are already grouped by destination; the per-expert
+   counts go to the host (they size the exchange) and are exchanged;
+3. the picked rows go out in one all_to_all_single, each rank runs its local
+   experts over what it received (the decode / grouped-GEMM kernels, with
+   the rows regrouped by local expert), and the expert outputs come back in a
+   second all_to_all_single;
+4. the weighted combine runs in each token's fixed k-slot order, so a
+   token's result does not depend on G.
+
+Only the routed rows cross NVLink.  The exchange plan is plain host code over
+the compute operations of an ``ops`` object: ``DeviceOps`` (this module)
+binds them to the library's CUDA kernels; tests drive the same plan with
+other ops over gloo on CPU.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import device as D
+from .layer import run_experts
+
+
+def local_plan(recv_ec: np.ndarray):
+    """Regroup received rows by local expert.
+
+    ``recv_ec[s, j]``: rows source rank s sent for local expert j, laid out
+    in the receive buffer source after source, each source's rows grouped by
+    expert in order.  Returns (counts (Eloc,), offsets (Eloc+1,), sorted_rows
+    (P,): the receive-buffer row of local pick q, local experts in order and
+    within an expert the sources in rank order, inv (P,): the local pick of
+    receive-buffer row p)."""
+    recv_ec = np.asarray(recv_ec, np.int64)
+    G, El = recv_ec.shape
+    src_off = np.concatenate([[0], np.cumsum(recv_ec.sum(axis=1))])
+    intra = np.concatenate([np.zeros((G, 1), np.int64), np.cumsum(recv_ec, axis=1)], axis=1)
+    counts = recv_ec.sum(axis=0)
+    offsets = np.concatenate([[0], np.cumsum(counts)])
+    parts = [np.arange(src_off[s] + intra[s, j], src_off[s] + intra[s, j] + recv_ec[s, j])
+             for j in range(El) for s in range(G)]
+    sorted_rows = np.concatenate(parts) if parts else np.zeros(0, np.int64)
+    inv = np.empty_like(sorted_rows)
+    inv[sorted_rows] = np.arange(len(sorted_rows))
+    return (counts.astype(np.int32), offsets.astype(np.int32), sorted_rows.astype(np.int32), inv.astype(np.int32))
+
+
+class EPLayer:
+    """One MoE layer with its E experts spread over the ranks of ``group``.
+
+    ``ops`` provides: ``route(x) -> (w (T*k,), counts (E,), sorted_rows (P,),
+    inv (P,))`` on the device, ``gather_rows(src, index) -> rows``,
+    ``experts(x_rows, counts, offsets, sorted_rows) -> y`` (the local experts,
+    y in local pick order), ``combine(y, inv, w, T, k) -> out`` and ``device``.
+    """
+
+    def __init__(self, ops, E: int, top_k: int, H: int, group=None):
+        self.ops, self.E, self.k, self.H, self.group = ops, E, top_k, H, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if E % self.world:
+            raise ValueError(f"E={E} experts do not split evenly over {self.world} ranks")
+        self.E_local = E // self.world
+        self.first_expert = self.rank * self.E_local
+
+    def _a2a(self, inp: torch.Tensor, out_rows, in_rows) -> torch.Tensor:
+        out = torch.empty((int(sum(out_rows)),) + tuple(inp.shape[1:]), dtype=inp.dtype, device=inp.device)
+        dist.all_to_all_single(out, inp, [int(v) for v in out_rows], [int(v) for v in in_rows], group=self.group)
+        return out
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        ops, G, El = self.ops, self.world, self.E_local
+        T = x.shape[0]
+        w, counts, sorted_rows, inv = ops.route(x)
+        send_ec = counts.reshape(G, El).to(torch.int32)
+        recv_ec_t = self._a2a(send_ec.contiguous(), [1] * G, [1] * G)          # row s: what rank s sends here
+        send_ec_h = send_ec.cpu().numpy().astype(np.int64)
+        recv_ec = recv_ec_t.cpu().numpy().astype(np.int64)
+        send_rows, recv_rows = send_ec_h.sum(axis=1), recv_ec.sum(axis=1)
+        xs = ops.gather_rows(x, sorted_rows)                                     # picks, grouped by destination
+        xr = self._a2a(xs, recv_rows, send_rows)
+        lc, lo, lsr, linv = local_plan(recv_ec)
+        dev = ops.device
+        y_local = ops.experts(xr, torch.from_numpy(lc).to(dev), torch.from_numpy(lo).to(dev),
+                              torch.from_numpy(lsr).to(dev))
+        yr = ops.gather_rows(y_local, torch.from_numpy(linv).to(dev))          # back to receive order
+        yb = self._a2a(yr, send_rows, recv_rows)                                 # my picks' outputs, sorted order
+        return ops.combine(yb, inv, w, T, self.k)
+
+    __call__ = forward
+
+
+class DeviceOps:
+    """The compute operations of EPLayer on this GPU's kernels.  ``experts``
+    is the rank's LayerExperts holding its E/G local experts as local ids
+    0 .. E/G-1 (global id = rank * E/G + local id)."""
+
+    def __init__(self, router: torch.Tensor, experts, E: int, top_k: int, normalize: bool = True,
+                 gemm_min_rows: int = 32):
+        self.router = router.contiguous()
+        self.experts = experts
+        self.E, self.k, self.normalize = E, top_k, normalize
+        self.gemm_min_rows = gemm_min_rows
+        self.device = router.device
+        self._ws = {}
+
+    def _buf(self, name, nbytes):
+        b = self._ws.get(name)
+        if b is None or b.numel() < nbytes:
+            b = self._ws[name] = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=self.device)
+        return b
+
+    def route(self, x):
+        T, H = x.shape
+        idx = torch.empty((T, self.k), dtype=torch.int32, device=self.device)
+        w = torch.empty((T, self.k), dtype=torch.float32, device=self.device)
+        rws = self._buf("router", D.router_workspace_bytes(T, H, self.E))
+        D.router_route(x, self.router, self.k, self.normalize, idx, w, workspace=rws)
+        r = D.permute(idx, w, self.E)
+        return w.view(-1), r.counts, r.sorted_rows[:r.P], r.inv[:r.P]
+
+    def gather_rows(self, src, index):
+        n = index.numel()
+        out = torch.empty((n, src.shape[1]), dtype=torch.float32, device=self.device)
+        if n:
+            ones = torch.ones(n, dtype=torch.float32, device=self.device)
+            D.combine(src, index.to(torch.int32).contiguous(), ones, n, 1, out=out)
+        return out
+
+    def experts(self, xr, counts, offsets, sorted_rows):
+        ex = self.experts
+        P, H = xr.shape
+        y = torch.empty((max(P, 1), H), dtype=torch.float32, device=self.device)
+        if P == 0:
+            return y[:0]
+        r = D.Routing.from_plan(counts, offsets, sorted_rows)
+        row_exp = D.row_exponents(xr)
+        status = self._ws.get("status")
+        if status is None:
+            status = self._ws["status"] = torch.zeros(1, dtype=torch.int32, device=self.device)
+        run_experts(ex, xr, row_exp, r, y, self._buf, status, self.gemm_min_rows)
+        return y[:P]
+
+    def combine(self, y, inv, w, T, k):
+        out = torch.empty((T, y.shape[1]), dtype=torch.float32, device=self.device)
+        return D.combine(y, inv, w, T, k, out=out)

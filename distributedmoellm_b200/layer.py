@@ -17,6 +17,35 @@ from . import device as D
 from .store import LayerExperts
 
 
+def uses_gemm(experts: LayerExperts, P: int, gemm_min_rows: int) -> bool:
+    """Whether the grouped-GEMM kernels run for P picks over these experts:
+    only when the picks average at least half of gemm_min_rows per expert
+    (prefill-sized batches) and the shape allows them (H % 128, I % 64)."""
+    m = gemm_min_rows
+    return (m > 0 and experts.H % 128 == 0 and experts.I % 64 == 0 and 2 * P >= experts.E * m
+            and P <= 65535 and not experts.missing_exp)
+
+
+def run_experts(experts: LayerExperts, x: torch.Tensor, row_exp: torch.Tensor, routing, y: torch.Tensor,
+                workspace, status: torch.Tensor, gemm_min_rows: int) -> None:
+    """Every expert's picks through its gate|up, SiLU, down into y (one row
+    per pick, in routing order): experts with at least gemm_min_rows picks as
+    grouped GEMMs on the tensor cores, the rest through the decode mat-vecs.
+    ``workspace(name, nbytes)`` returns a uint8 device buffer of at least
+    nbytes that stays the same between calls of the same size."""
+    ex, P = experts, routing.P
+    if uses_gemm(ex, P, gemm_min_rows):
+        D.moe_decode(ex.table, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing, y,
+                     workspace("decode", D.decode_workspace_bytes(P, ex.I)), max_rows=gemm_min_rows - 1,
+                     status=status)
+        D.moe_prefill(ex.table, ex.eexp, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing, y,
+                      workspace("prefill", D.prefill_workspace_bytes(P, ex.H, ex.I)), min_rows=gemm_min_rows,
+                      status=status)
+    else:
+        D.moe_decode(ex.table, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing, y,
+                     workspace("decode", D.decode_workspace_bytes(P, ex.I)), max_rows=0, status=status)
+
+
 class _Buffers:
     def __init__(self, T: int, E: int, k: int, H: int, I: int, dev):
         P = T * k
@@ -54,9 +83,7 @@ class MoELayer:
         self._bufs: dict[int, _Buffers] = {}
 
     def uses_gemm(self, T: int) -> bool:
-        m = self.gemm_min_rows
-        return (m > 0 and self.H % 128 == 0 and self.I % 64 == 0 and 2 * T * self.k >= self.E * m
-                and T * self.k <= 65535 and not self.experts.missing_exp)
+        return uses_gemm(self.experts, T * self.k, self.gemm_min_rows)
 
     def buffers(self, T: int) -> _Buffers:
         b = self._bufs.get(T)
@@ -71,19 +98,13 @@ class MoELayer:
         return b
 
     def experts_forward(self, x: torch.Tensor, b: _Buffers) -> None:
-        ex = self.experts
-        T = x.shape[0]
-        if self.uses_gemm(T):
+        def workspace(name, nbytes):
+            if name == "decode":
+                return b.ws
             if b.pws is None:
-                b.pws = torch.empty(D.prefill_workspace_bytes(T * self.k, self.H, self.I), dtype=torch.uint8,
-                                    device=x.device)
-            D.moe_decode(ex.table, self.E, self.H, self.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, b.row_exp, b.routing,
-                         b.y, b.ws, max_rows=self.gemm_min_rows - 1, status=b.status)
-            D.moe_prefill(ex.table, ex.eexp, self.E, self.H, self.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, b.row_exp,
-                          b.routing, b.y, b.pws, min_rows=self.gemm_min_rows, status=b.status)
-        else:
-            D.moe_decode(ex.table, self.E, self.H, self.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, b.row_exp, b.routing,
-                         b.y, b.ws, max_rows=0, status=b.status)
+                b.pws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+            return b.pws
+        run_experts(self.experts, x, b.row_exp, b.routing, b.y, workspace, b.status, self.gemm_min_rows)
 
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """out (T, H) = sum over each token's k picks of weight * expert(x)."""

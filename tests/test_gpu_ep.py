@@ -1,0 +1,111 @@
+"""Expert parallelism on 2 GPUs: NCCL ranks run ep.EPLayer over the
+library's kernels (each rank holding half of the experts) and every rank's
+output must match one GPU running the whole layer over all ranks' tokens
+(1e-5 of each row's max on the decode path, 2e-3 when the grouped GEMMs run).
+Skipped with fewer than 2 GPUs."""
+
+import datetime
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _setup(E, H, I, seed=9):
+    from distributedmoellm_b200 import synthetic as S
+    rng = np.random.default_rng(seed)
+    parts = {e: S.int4_expert(rng, H, I, 32, f16_scales=True) for e in range(E)}
+    router = S.router(rng, E, H)
+    return parts, router
+
+
+def _tokens(rank, T, H):
+    return np.random.default_rng(500 + rank).standard_normal((T, H), dtype=np.float32)
+
+
+def _worker(rank, world, port, q, E, H, I, T):
+    try:
+        sys.path.insert(0, str(ROOT))
+        import torch
+        import torch.distributed as dist
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+        from distributedmoellm_b200 import layout as L
+        from distributedmoellm_b200.ep import DeviceOps, EPLayer
+        from distributedmoellm_b200.layer import MoELayer
+        from distributedmoellm_b200.store import LayerExperts
+        parts, router = _setup(E, H, I)
+        El = E // world
+        local = LayerExperts(El, H, I, 32, L.FMT_Q4_F16, L.FMT_Q4_F16, dev)
+        for j in range(El):
+            local.put_int4(j, *parts[rank * El + j])
+        local.publish()
+        rt = torch.from_numpy(router).to(dev)
+        layer = EPLayer(DeviceOps(rt, local, E, 2), E, 2, H)
+        x = torch.from_numpy(_tokens(rank, T, H)).to(dev)
+        out = layer(x).cpu().numpy()
+        out2 = layer(x).cpu().numpy()
+        ref = None
+        if rank == 0:                  # the whole layer on one GPU over every rank's tokens
+            full = LayerExperts(E, H, I, 32, L.FMT_Q4_F16, L.FMT_Q4_F16, dev)
+            for e in range(E):
+                full.put_int4(e, *parts[e])
+            full.publish()
+            ml = MoELayer(rt, full, 2, True)
+            xa = np.concatenate([_tokens(r, T, H) for r in range(world)])
+            ref = ml(torch.from_numpy(xa).to(dev)).cpu().numpy()
+            ref = (ref, ml.uses_gemm(len(xa)))
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok", (out, out2, ref)))
+    except Exception as exc:
+        q.put((rank, "exception", repr(exc)))
+
+
+@pytest.mark.parametrize("E,H,I,T,tol", [(8, 256, 256, 24, 1e-5), (8, 512, 256, 512, 2e-3)],
+                         ids=["decode", "grouped_gemm"])
+def test_ep_two_gpus_match_one_gpu(E, H, I, T, tol):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, E, H, I, T)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(2):
+            r, kind, val = q.get(timeout=300)
+            res[r] = (kind, val)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert all(res[r][0] == "ok" for r in range(2)), {r: res[r][1] for r in res if res[r][0] != "ok"}
+    ref, gemm = res[0][1][2]
+    assert gemm == (T > 100)
+    for r in range(2):
+        out, out2 = res[r][1][0], res[r][1][1]
+        want = ref[r * T:(r + 1) * T]
+        err = float((np.abs(out - want).max(axis=1) / np.abs(want).max(axis=1)).max())
+        assert err < tol, (r, err)
+        assert np.array_equal(out, out2)
