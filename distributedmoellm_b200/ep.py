@@ -109,7 +109,7 @@ class DeviceOps:
     def __init__(self, router: torch.Tensor, experts, E: int, top_k: int, normalize: bool = True,
                  gemm_min_rows: int = 32):
         self.router = router.contiguous()
-        self.experts = experts
+        self.store = experts
         self.E, self.k, self.normalize = E, top_k, normalize
         self.gemm_min_rows = gemm_min_rows
         self.device = router.device
@@ -139,7 +139,7 @@ class DeviceOps:
         return out
 
     def experts(self, xr, counts, offsets, sorted_rows):
-        ex = self.experts
+        ex = self.store
         P, H = xr.shape
         y = torch.empty((max(P, 1), H), dtype=torch.float32, device=self.device)
         if P == 0:

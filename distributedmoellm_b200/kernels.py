@@ -1,0 +1,172 @@
+"""moelan.kernels' expert entry points on the GPU, same signatures.
+
+Mirrors moelan/kernels.py:930-1032: numpy arrays in, numpy arrays out (the
+call copies its inputs to the current CUDA device, runs this library's
+kernels and copies the result back), so ``install()`` can put them in place of
+the reference's numba kernels behind ExpertStore, Packed4, GroupQuant and
+gguf.QuantMatrix unchanged.  Dequantisation is bit-exact; the products match
+the reference's f32 path within 1e-5 of each output row's largest magnitude.
+
+Weight matrices are packed into the device tile layout on first use and kept
+(keyed by the arrays' addresses, shapes and dtypes, holding a reference so
+the address cannot be reused while cached): like the reference's resident
+experts (kernels.py:942-947), they must not change while they are in use.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from collections import OrderedDict
+
+import numpy as np
+import torch
+
+from . import device as D
+from . import layout
+from .accel import DevicePool
+from .packing import Packed
+
+_CACHE_MAX = 512
+_mats: OrderedDict = OrderedDict()        # matrix key -> (device tiles, fmt, O, K, kept arrays)
+_pool: dict = {}                          # device index -> DevicePool of moe_q4 experts
+_pool_keys: OrderedDict = OrderedDict()
+
+
+def _dev():
+    D.require_device()
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def _key(*arrays):
+    return tuple((a.__array_interface__["data"][0], a.shape, a.dtype.str, a.strides) for a in arrays)
+
+
+def _tiles(key, make, keep):
+    hit = _mats.get(key)
+    if hit is not None:
+        _mats.move_to_end(key)
+        return hit
+    fmt, O, K, tiles = make()
+    ent = (torch.from_numpy(tiles).to(_dev()), fmt, O, K, keep)
+    _mats[key] = ent
+    while len(_mats) > _CACHE_MAX:
+        _mats.popitem(last=False)
+    return ent
+
+
+def _matmul(ent, x):
+    t, fmt, O, K, _ = ent
+    xd = torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(t.device)
+    return D.matmul_t(t, fmt, O, K, xd).cpu().numpy()
+
+
+# ---- dequantisation (moelan/kernels.py:971-1003) ------------------------------------
+
+def q4_dequant(raw, s, gs: int, offset: bool, out: np.ndarray) -> np.ndarray:
+    dev = _dev()
+    r = torch.from_numpy(np.ascontiguousarray(raw, np.uint8)).to(dev)
+    sc = torch.from_numpy(np.ascontiguousarray(s)).to(dev)
+    out[...] = D.q4_dequant(r, sc, gs, offset).cpu().numpy()
+    return out
+
+
+def q8_dequant(q, s, gs: int, out: np.ndarray) -> np.ndarray:
+    dev = _dev()
+    qq = torch.from_numpy(np.ascontiguousarray(q, np.int8)).to(dev)
+    sc = torch.from_numpy(np.ascontiguousarray(s)).to(dev)
+    out[...] = D.q8_dequant(qq, sc, gs).cpu().numpy()
+    return out
+
+
+def gguf_dequant(raw: np.ndarray, qtype: int, out: np.ndarray) -> np.ndarray:
+    r = torch.from_numpy(np.ascontiguousarray(raw, np.uint8)).to(_dev())
+    out[...] = D.gguf_dequant(r, int(qtype), out.shape[1]).cpu().numpy()
+    return out
+
+
+# ---- single matrices: x @ W.T (moelan/kernels.py:981-998, 1018-1032) ----------------
+
+def q4_matmul_t(x: np.ndarray, raw: np.ndarray, s: np.ndarray, gs: int, offset: bool) -> np.ndarray:
+    """x @ W.T for colibri int4 bytes; ``offset`` means raw was XOR-ed with 0x88."""
+    def make():
+        O, K = raw.shape[0], raw.shape[1] * 2
+        return layout.fmt_of("q4", s), O, K, layout.q4_tiles(raw, s, gs, offset)
+    return _matmul(_tiles(_key(raw, s) + (gs, bool(offset)), make, (raw, s)), x)
+
+
+def q8_matmul_t(x: np.ndarray, q: np.ndarray, s: np.ndarray, gs: int) -> np.ndarray:
+    def make():
+        return layout.fmt_of("q8", s), q.shape[0], q.shape[1], layout.q8_tiles(q, s, gs)
+    return _matmul(_tiles(_key(q, s) + (gs,), make, (q, s)), x)
+
+
+def gguf_matmul_t(x: np.ndarray, raw: np.ndarray, qtype: int, cols: int) -> np.ndarray:
+    """x @ W.T for GGUF blocks: Q8_0 and Q4_0 (as int8 / int4 tiles with their
+    f16 block scales)."""
+    if qtype == 8:
+        def make():
+            q, d = layout.q8_0_as_q8(raw, cols)
+            return layout.FMT_Q8_F16, raw.shape[0], cols, layout.q8_tiles(q, d, 32)
+    elif qtype == 2:
+        def make():
+            r, d = layout.q4_0_as_q4(raw, cols)
+            return layout.FMT_Q4_F16, raw.shape[0], cols, layout.q4_tiles(r, d, 32, True)
+    else:
+        raise RuntimeError(f"gguf_matmul_t: GGUF type {qtype} has no device tile format in this build")
+    return _matmul(_tiles(_key(raw) + (int(qtype), cols), make, (raw,)), x)
+
+
+# ---- the fused int4 layer call (moelan/kernels.py:930-968) ------------------------------
+
+def q4_expert_ptrs(e) -> tuple[int, int, int, int, int] | None:
+    """What :func:`moe_q4` needs of one int4 expert (addresses of its four
+    arrays and the XOR for its nibbles), or None if it does not qualify; the
+    same rule as the reference (kernels.py:930-939)."""
+    gu, dn = e.gu, e.down
+    for m in (gu, dn):
+        if not (hasattr(m, "raw") and hasattr(m, "offset") and m.raw.flags.c_contiguous
+                and m.s.flags.c_contiguous and m.raw.dtype == np.uint8 and m.s.dtype == np.float32):
+            return None
+    if gu.gs != dn.gs or gu.offset != dn.offset:
+        return None
+    addr = lambda a: a.__array_interface__["data"][0]   # noqa: E731
+    return addr(gu.raw), addr(gu.s), addr(dn.raw), addr(dn.s), 0 if gu.offset else 0x88
+
+
+def _from_address(addr: int, n: int, dtype) -> np.ndarray:
+    ct = {np.uint8: ctypes.c_uint8, np.float32: ctypes.c_float}[dtype]
+    return np.ctypeslib.as_array((ct * n).from_address(addr))
+
+
+def moe_q4(x: np.ndarray, items, H: int, I: int, gs: int, out: np.ndarray) -> None:
+    """Add ``sum_e w * expert_e(x[rows])`` into ``out`` for colibri int4
+    experts in one call.  ``items``: (ptrs from :func:`q4_expert_ptrs`, rows,
+    gate weights) per expert; the arrays behind the pointers must stay alive
+    and unchanged (each expert is uploaded on first use and kept)."""
+    dev = _dev()
+    pool = _pool.get(dev.index)
+    if pool is None:
+        pool = _pool[dev.index] = DevicePool(dev)
+    keys = []
+    for ptrs, _, _ in items:
+        key = (tuple(int(p) for p in ptrs), H, I, gs)
+        if key not in pool.entries:
+            g_raw = _from_address(ptrs[0], 2 * I * H // 2, np.uint8).reshape(2 * I, H // 2)
+            g_s = _from_address(ptrs[1], 2 * I * (H // gs), np.float32).reshape(2 * I, H // gs)
+            d_raw = _from_address(ptrs[2], H * I // 2, np.uint8).reshape(H, I // 2)
+            d_s = _from_address(ptrs[3], H * (I // gs), np.float32).reshape(H, I // gs)
+            off = int(ptrs[4]) == 0
+            eexp = (layout.weight_exponent(g_s, 8), layout.weight_exponent(d_s, 8),
+                    layout.act_exponent(layout.row_l1_q4(g_raw, g_s, gs, off), I))
+            pool.put(key, Packed(layout.FMT_Q4_F32, layout.FMT_Q4_F32, gs, H, I,
+                                 layout.q4_tiles(g_raw, g_s, gs, off, gu_inter=I), layout.q4_tiles(d_raw, d_s, gs, off),
+                                 eexp))
+            _pool_keys[key] = None
+            while len(_pool_keys) > _CACHE_MAX:
+                pool.pop(_pool_keys.popitem(last=False)[0])
+        keys.append(key)
+    xd = torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(dev)
+    uniq, part, status = pool.compute(xd, keys, [r for _, r, _ in items], [w for _, _, w in items])
+    out[uniq] += part.cpu().numpy()
+    if int(status.item()):
+        raise RuntimeError(f"moe_q4: the GPU kernels reported status {int(status.item())}")

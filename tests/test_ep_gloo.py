@@ -165,3 +165,13 @@ def test_ep_rank_failure_surfaces_as_an_error():
     res = _run(2, fail_rank=1)
     assert res[1][0] == "raised", res
     assert res[0][0] in ("error", "exception"), res
+
+
+def test_device_ops_expose_every_operation_ep_uses():
+    sys.path.insert(0, str(ROOT))
+    import torch
+    from distributedmoellm_b200.ep import DeviceOps
+    ops = DeviceOps(torch.zeros((E, H)), object(), E, K)
+    for name in ("route", "gather_rows", "experts", "combine"):
+        assert callable(getattr(ops, name)), name
+    assert ops.device == torch.device("cpu")

@@ -1,0 +1,129 @@
+"""GPU tests of the drop-in (distributedmoellm_b200.kernels / accel): the
+same calls moelan makes, on duck-typed stand-ins for its matrix objects
+(Packed4, GroupQuant, gguf.QuantMatrix), checked against the CPU oracle.
+Bars: dequantisation bit-exact; f32 mat-vec paths 1e-5 of each row's max."""
+
+import types
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+NS = types.SimpleNamespace
+TOL = 1e-5
+
+
+@pytest.fixture(scope="module")
+def K():
+    from distributedmoellm_b200 import _build
+    _build.build()
+    from distributedmoellm_b200 import device, kernels
+    device.require_device()
+    return kernels
+
+
+def row_err(got, want):
+    got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
+    return float((np.abs(got - want).max(axis=1) / np.maximum(np.abs(want).max(axis=1), 1e-30)).max())
+
+
+def packed4(raw, s, gs, offset=False):
+    return NS(raw=np.ascontiguousarray(raw), s=np.ascontiguousarray(s), gs=gs, offset=offset,
+              shape=(raw.shape[0], raw.shape[1] * 2))
+
+
+def int4_expert(rng, H, I, gs=32, f16=False):
+    from distributedmoellm_b200 import synthetic as S
+    gr, gsc, dr, dsc = S.int4_expert(rng, H, I, gs, f16_scales=f16)
+    e = NS(gu=packed4(gr, gsc, gs), down=packed4(dr, dsc, gs), inter=I)
+    desc = (("q4", gr, gsc.astype(np.float32), gs, False), ("q4", dr, dsc.astype(np.float32), gs, False))
+    return e, desc
+
+
+def test_dequant_entry_points_bit_exact(K):
+    from distributedmoellm_b200 import synthetic as S
+    rng = np.random.default_rng(0)
+    gr, gsc, _, _ = S.int4_expert(rng, 256, 128, 32, f16_scales=False)
+    out = np.empty((256, 256), np.float32)
+    assert K.q4_dequant(gr, gsc, 32, False, out) is out
+    assert np.array_equal(out.view(np.uint32), O.q4_dequant(gr, gsc, 32, False).view(np.uint32))
+    q, s, _, _ = S.int8_expert(rng, 128, 128, 32)
+    out8 = np.empty(q.shape, np.float32)
+    K.q8_dequant(q, s, 32, out8)
+    assert np.array_equal(out8, O.q8_dequant(q, s, 32))
+    raw = S.gguf_rows(rng, 16, 512, 12)
+    og = np.empty((16, 512), np.float32)
+    K.gguf_dequant(raw, 12, og)
+    assert np.array_equal(og, O.gguf_dequant(raw, 12, 512))
+
+
+@pytest.mark.parametrize("n", [1, 3, 9])
+def test_matmul_entry_points(K, n):
+    from distributedmoellm_b200 import synthetic as S
+    rng = np.random.default_rng(n)
+    x = rng.standard_normal((n, 512), dtype=np.float32)
+    gr, gsc, _, _ = S.int4_expert(rng, 512, 128, 32, f16_scales=False)
+    assert row_err(K.q4_matmul_t(x, gr, gsc, 32, False), O.q4_matmul_t(x, gr, gsc, 32, False)) < TOL
+    assert row_err(K.q4_matmul_t(x, gr, gsc, 32, False), O.q4_matmul_t(x, gr, gsc, 32, False)) < TOL   # cached
+    q, s, _, _ = S.int8_expert(rng, 512, 128, 32)
+    assert row_err(K.q8_matmul_t(x, q, s, 32), O.q8_matmul_t(x, q, s, 32)) < TOL
+    for qt in (8, 2):
+        raw = S.gguf_rows(rng, 96, 512, qt)
+        assert row_err(K.gguf_matmul_t(x, raw, qt, 512), O.gguf_matmul_t(x, raw, qt, 512)) < TOL
+
+
+def test_moe_q4_matches_the_reference_kernel(K):
+    rng = np.random.default_rng(7)
+    H, I, gs, T = 512, 256, 32, 12
+    experts = [int4_expert(rng, H, I, gs) for _ in range(5)]
+    x = rng.standard_normal((T, H), dtype=np.float32)
+    items = []
+    for j, (e, desc) in enumerate(experts):
+        rows = np.sort(rng.choice(T, size=2 + j, replace=False)).astype(np.int64)
+        w = rng.random(len(rows), dtype=np.float32)
+        ptrs = K.q4_expert_ptrs(e)
+        assert ptrs is not None and ptrs[4] == 0x88
+        items.append((ptrs, rows, w))
+    out = rng.standard_normal((T, H), dtype=np.float32)
+    want = out.copy()
+    O.moe_q4(x, items, H, I, gs, want)
+    for _ in range(2):              # the second call reuses the uploaded experts
+        got = out.copy()
+        K.moe_q4(x, items, H, I, gs, got)
+        assert row_err(got, want) < TOL
+
+
+def test_gpu_tier_launch_collect_and_stats():
+    from distributedmoellm_b200.accel import GpuTier, bench_gpu
+    rng = np.random.default_rng(11)
+    H, I = 256, 256
+    tier = GpuTier("cuda", 64 << 20)
+    experts = {e: int4_expert(rng, H, I, f16=(e % 2 == 1)) for e in range(4)}
+    for e, (ex, _) in experts.items():
+        assert tier.add((3, e), ex)
+    assert (3, 1) in tier and (4, 1) not in tier
+    dense = NS(gu=NS(w=np.zeros((2 * I, H), np.float32)), down=NS(w=np.zeros((H, I), np.float32)), inter=I)
+    assert not tier.add((3, 9), dense)
+    x = rng.standard_normal((20, H), dtype=np.float32)
+    groups = [(e, np.sort(rng.choice(20, size=3 + e, replace=False)), rng.random(3 + e, dtype=np.float32))
+              for e in range(4)] + [(7, np.array([0, 1]), np.ones(2, np.float32))]
+    handle, rest = tier.launch_held(3, x, groups)
+    assert [g[0] for g in rest] == [7]
+    out = np.ones((20, H), np.float32)
+    tier.collect(handle, out)
+    want = np.ones((20, H), np.float32)
+    for e, rows, w in groups[:4]:
+        want[rows] += O.expert_forward(x[rows], *experts[e][1], I) * w[:, None]
+    assert row_err(out - 1.0, want - 1.0) < TOL
+    st = tier.stats()
+    assert set(st) == {"device", "experts", "used_bytes", "budget_bytes", "share", "gpu_ms_per_expert",
+                       "cpu_ms_per_expert", "calls", "busy_s"}
+    assert st["experts"] == 4 and st["calls"] == 1 and st["used_bytes"] == tier.used > 0
+    tier.release()
+    assert tier.used == 0 and not tier.experts
+    share = tier.calibrate(experts[0][0], lambda xx: O.expert_forward(xx, *experts[0][1], I), H)
+    assert 0.0 < share < 1.0 and tier.used == 0
+    b = bench_gpu("cuda", 1 << 30, H, I, "int4", 32, make_expert=lambda h, i, f, g: int4_expert(rng, h, i, g)[0])
+    assert b["gpu_experts"] > 0 and b["gpu_ms"] > 0

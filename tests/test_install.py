@@ -1,0 +1,126 @@
+"""The drop-in on CPU: packing of moelan's matrix objects into the tile
+layout, and install() patching (it must refuse, patching nothing, without an
+sm_100 device; with the device check bypassed it replaces exactly the
+reference's expert entry points and uninstall() restores them)."""
+
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+
+from distributedmoellm_b200 import layout as L  # noqa: E402
+from distributedmoellm_b200 import synthetic as S  # noqa: E402
+from distributedmoellm_b200.packing import pack_expert  # noqa: E402
+
+NS = types.SimpleNamespace
+
+
+def packed4(raw, s, gs, offset=False):
+    return NS(raw=raw, s=s, gs=gs, offset=offset, shape=(raw.shape[0], raw.shape[1] * 2))
+
+
+def test_pack_int4_expert_matches_the_tile_layout():
+    rng = np.random.default_rng(0)
+    gr, gsc, dr, dsc = S.int4_expert(rng, 256, 128, 32, f16_scales=False)
+    p = pack_expert(NS(gu=packed4(gr, gsc, 32), down=packed4(dr, dsc, 32), inter=128))
+    assert (p.fmt_gu, p.gs, p.H, p.I) == (L.FMT_Q4_F32, 32, 256, 128)
+    assert np.array_equal(p.gu_tiles, L.q4_tiles(gr, gsc, 32, False, gu_inter=128))
+    assert np.array_equal(p.dn_tiles, L.q4_tiles(dr, dsc, 32, False))
+    assert p.eexp[0] == L.weight_exponent(gsc, 8)
+
+
+def test_pack_int8_and_gguf_and_stacked():
+    rng = np.random.default_rng(1)
+    gq, gs_, dq, ds = S.int8_expert(rng, 256, 128, 32)
+    p = pack_expert(NS(gu=NS(q=gq, s=gs_, gs=32), down=NS(q=dq, s=ds, gs=32), inter=128))
+    assert p.fmt_gu == L.FMT_Q8_F32 and np.array_equal(p.dn_tiles, L.q8_tiles(dq, ds, 32))
+    g = NS(raw=S.gguf_rows(rng, 128, 256, 8), qtype=8, shape=(128, 256))
+    u = NS(raw=S.gguf_rows(rng, 128, 256, 8), qtype=8, shape=(128, 256))
+    d = NS(raw=S.gguf_rows(rng, 256, 128, 8), qtype=8, shape=(256, 128))
+    p = pack_expert(NS(gu=NS(parts=(g, u)), down=d, inter=128))
+    q, sc = L.q8_0_as_q8(np.concatenate([g.raw, u.raw]), 256)
+    assert p.fmt_gu == L.FMT_Q8_F16 and np.array_equal(p.gu_tiles, L.q8_tiles(q, sc, 32, gu_inter=128))
+    q40 = NS(raw=S.gguf_rows(rng, 256, 128, 2), qtype=2, shape=(256, 128))
+    gu40 = NS(raw=S.gguf_rows(rng, 256, 256, 2), qtype=2, shape=(256, 256))
+    assert pack_expert(NS(gu=gu40, down=q40, inter=128)).fmt_down == L.FMT_Q4_F16
+
+
+def test_pack_refuses_dense_and_mixed():
+    rng = np.random.default_rng(2)
+    gr, gsc, dr, dsc = S.int4_expert(rng, 256, 128, 32, f16_scales=False)
+    dense = NS(w=np.zeros((256, 128), np.float32))
+    assert pack_expert(NS(gu=packed4(gr, gsc, 32), down=dense, inter=128)) is None
+    gq, gs_, dq, ds = S.int8_expert(rng, 256, 128, 32)
+    assert pack_expert(NS(gu=packed4(gr, gsc, 32), down=NS(q=dq, s=ds, gs=32), inter=128)) is None
+    q4k = NS(raw=S.gguf_rows(rng, 256, 256, 12), qtype=12, shape=(256, 256))
+    assert pack_expert(NS(gu=q4k, down=q4k, inter=128)) is None
+
+
+def _fake_moelan():
+    k = types.ModuleType("fake_moelan.kernels")
+    a = types.ModuleType("fake_moelan.accel")
+    from distributedmoellm_b200.install import ACCEL_NAMES, KERNEL_NAMES
+    for n in KERNEL_NAMES:
+        setattr(k, n, ("orig", n))
+    for n in ACCEL_NAMES:
+        setattr(a, n, ("orig", n))
+    pkg = types.ModuleType("fake_moelan")
+    pkg.kernels, pkg.accel = k, a
+    return pkg
+
+
+def test_install_refuses_without_a_device():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is present")
+    from distributedmoellm_b200.install import install
+    pkg = _fake_moelan()
+    with pytest.raises(RuntimeError):
+        install(pkg)
+    assert pkg.kernels.moe_q4 == ("orig", "moe_q4")
+
+
+def test_install_patches_and_uninstall_restores(monkeypatch):
+    from distributedmoellm_b200 import accel, device, kernels
+    from distributedmoellm_b200.install import ACCEL_NAMES, KERNEL_NAMES, install, uninstall
+    monkeypatch.setattr(device, "require_device", lambda: None)
+    pkg = _fake_moelan()
+    saved = install(pkg)
+    for n in KERNEL_NAMES:
+        assert getattr(pkg.kernels, n) is getattr(kernels, n)
+    for n in ACCEL_NAMES:
+        assert getattr(pkg.accel, n) is getattr(accel, n)
+    uninstall(saved)
+    assert pkg.kernels.moe_q4 == ("orig", "moe_q4") and pkg.accel.GpuTier == ("orig", "GpuTier")
+
+
+REF = Path("/root/reference")
+
+
+@pytest.mark.skipif(not (REF / "moelan").is_dir(), reason="the reference is not present here")
+def test_install_covers_the_reference_entry_points(monkeypatch):
+    """Every name install() replaces exists in the reference's modules with
+    the same parameters (so moelan's callers bind to ours unchanged)."""
+    import inspect
+    monkeypatch.setattr(sys, "dont_write_bytecode", True)       # nothing is written next to the reference
+    monkeypatch.syspath_prepend(str(REF))
+    monkeypatch.setenv("NUMBA_CACHE_DIR", "/tmp/numba_cache")
+    mk = pytest.importorskip("moelan.kernels")
+    ma = pytest.importorskip("moelan.accel")
+    from distributedmoellm_b200 import accel, kernels
+    from distributedmoellm_b200.install import ACCEL_NAMES, KERNEL_NAMES
+    for mod, ours, names in ((mk, kernels, KERNEL_NAMES), (ma, accel, ACCEL_NAMES)):
+        for n in names:
+            ref = getattr(mod, n)
+            mine = getattr(ours, n)
+            rp = list(inspect.signature(ref).parameters)
+            mp_ = list(inspect.signature(mine).parameters)
+            assert mp_[:len(rp)] == rp, (n, rp, mp_)
+    for m in ("expert_bytes", "add", "launch", "launch_held", "release", "collect", "calibrate", "stats"):
+        assert list(inspect.signature(getattr(ma.GpuTier, m)).parameters) == \
+            list(inspect.signature(getattr(accel.GpuTier, m)).parameters), m
