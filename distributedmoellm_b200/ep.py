@@ -21,6 +21,15 @@ Only the routed rows cross NVLink.  The exchange plan is plain host code over
 the compute operations of an ``ops`` object: ``DeviceOps`` (this module)
 binds them to the library's CUDA kernels; tests drive the same plan with
 other ops over gloo on CPU.
+
+``EPGatherLayer`` is the form for decode-sized batches, where the host round
+trip of the exchange plan would cost more than the experts: every rank
+all-gathers the tokens, routes all of them (the same kernels on the same
+data give every rank the same routing), runs its own expert slice over the
+picks that fall in it, sums each token's local picks (the other picks are
+skipped) and a reduce-scatter adds the ranks' partial sums.  All sizes are
+fixed by T, nothing goes through the host, and the step can be captured in a
+CUDA graph, collectives included.
 """
 
 from __future__ import annotations
@@ -155,3 +164,91 @@ class DeviceOps:
     def combine(self, y, inv, w, T, k):
         out = torch.empty((T, y.shape[1]), dtype=torch.float32, device=self.device)
         return D.combine(y, inv, w, T, k, out=out)
+
+
+class _GatherBuffers:
+    def __init__(self, T, world, E, k, H, I, dev):
+        TA, P = T * world, T * world * k
+        self.x_all = torch.empty((TA, H), dtype=torch.float32, device=dev)
+        self.row_exp = torch.empty(TA, dtype=torch.int32, device=dev)
+        self.idx = torch.empty((TA, k), dtype=torch.int32, device=dev)
+        self.w = torch.empty((TA, k), dtype=torch.float32, device=dev)
+        self.routing = D.Routing(TA, k, E, dev)
+        self.rws = torch.empty(D.router_workspace_bytes(TA, H, E), dtype=torch.uint8, device=dev)
+        self.y = torch.empty((max(P, 1), H), dtype=torch.float32, device=dev)
+        self.inv_local = torch.empty(max(P, 1), dtype=torch.int32, device=dev)
+        self.partial = torch.empty((TA, H), dtype=torch.float32, device=dev)
+        self.out = torch.empty((T, H), dtype=torch.float32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.ws = {}
+
+    def workspace(self, name, nbytes):
+        b = self.ws.get(name)
+        if b is None or b.numel() < nbytes:
+            b = self.ws[name] = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=self.out.device)
+        return b
+
+
+class EPGatherLayer:
+    """One MoE layer over the ranks of ``group`` for decode-sized batches:
+    all-gather of the tokens, replicated routing, the rank's own experts
+    (``experts``: its E/G local experts as local ids 0 .. E/G-1), combine of
+    its picks, reduce-scatter of the partial sums.  Token results equal the
+    one-GPU layer's up to the order of the final sum over ranks."""
+
+    def __init__(self, router: torch.Tensor, experts, E: int, top_k: int, normalize: bool = True, group=None,
+                 gemm_min_rows: int = 32):
+        self.router = router.contiguous()
+        self.experts, self.E, self.k, self.normalize, self.group = experts, E, top_k, normalize, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if E % self.world or experts.E != E // self.world:
+            raise ValueError(f"E={E} experts do not split into {self.world} slices of {experts.E}")
+        self.E_local = E // self.world
+        self.first_expert = self.rank * self.E_local
+        self.gemm_min_rows = gemm_min_rows
+        self._bufs: dict = {}
+
+    def buffers(self, T: int) -> _GatherBuffers:
+        b = self._bufs.get(T)
+        if b is None:
+            ex = self.experts
+            b = self._bufs[T] = _GatherBuffers(T, self.world, self.E, self.k, ex.H, ex.I, self.router.device)
+        return b
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        T = x.shape[0]
+        b = self.buffers(T)
+        e0, El, k = self.first_expert, self.E_local, self.k
+        dist.all_gather_into_tensor(b.x_all, x.contiguous(), group=self.group)
+        D.router_route(b.x_all, self.router, k, self.normalize, b.idx, b.w, row_exp=b.row_exp, workspace=b.rws)
+        r = D.permute(b.idx, b.w, self.E, b.routing)
+        P = r.P
+        local = D.Routing.from_plan(r.counts[e0:e0 + El], r.offsets[e0:e0 + El + 1], r.sorted_rows[:P])
+        run_experts(self.experts, b.x_all, b.row_exp, local, b.y, b.workspace, b.status, self.gemm_min_rows,
+                    picks=P // self.world)
+        # the other ranks' picks are skipped by the combine (pick index -1)
+        mine = (b.idx.view(-1) >= e0) & (b.idx.view(-1) < e0 + El)
+        torch.where(mine, r.inv[:P], torch.full_like(r.inv[:P], -1), out=b.inv_local[:P])
+        D.combine(b.y, b.inv_local[:P], b.w.view(-1), T * self.world, k, out=b.partial)
+        dist.reduce_scatter_tensor(b.out, b.partial, group=self.group)
+        return b.out
+
+    __call__ = forward
+
+    def capture(self, x: torch.Tensor) -> torch.cuda.CUDAGraph:
+        """A CUDA graph of forward(x), collectives included, on x's current
+        contents; replay it after writing new inputs into x.  Output:
+        buffers(T).out.  Release the graph before destroying the process group."""
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self.forward(x)
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.forward(x)
+        return g
+
+    def status(self, T: int) -> int:
+        return int(self.buffers(T).status.item())

@@ -27,14 +27,16 @@ def uses_gemm(experts: LayerExperts, P: int, gemm_min_rows: int) -> bool:
 
 
 def run_experts(experts: LayerExperts, x: torch.Tensor, row_exp: torch.Tensor, routing, y: torch.Tensor,
-                workspace, status: torch.Tensor, gemm_min_rows: int) -> None:
+                workspace, status: torch.Tensor, gemm_min_rows: int, picks: int | None = None) -> None:
     """Every expert's picks through its gate|up, SiLU, down into y (one row
     per pick, in routing order): experts with at least gemm_min_rows picks as
     grouped GEMMs on the tensor cores, the rest through the decode mat-vecs.
     ``workspace(name, nbytes)`` returns a uint8 device buffer of at least
-    nbytes that stays the same between calls of the same size."""
+    nbytes that stays the same between calls of the same size.  ``picks``:
+    the picks these experts get (default routing.P; smaller when routing
+    covers other ranks' experts too), for the choice of kernels."""
     ex, P = experts, routing.P
-    if uses_gemm(ex, P, gemm_min_rows):
+    if uses_gemm(ex, P if picks is None else picks, gemm_min_rows):
         D.moe_decode(ex.table, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing, y,
                      workspace("decode", D.decode_workspace_bytes(P, ex.I)), max_rows=gemm_min_rows - 1,
                      status=status)

@@ -35,7 +35,7 @@ def _tokens(rank, T, H):
     return np.random.default_rng(500 + rank).standard_normal((T, H), dtype=np.float32)
 
 
-def _worker(rank, world, port, q, E, H, I, T):
+def _worker(rank, world, port, q, E, H, I, T, mode):
     try:
         sys.path.insert(0, str(ROOT))
         import torch
@@ -56,10 +56,21 @@ def _worker(rank, world, port, q, E, H, I, T):
             local.put_int4(j, *parts[rank * El + j])
         local.publish()
         rt = torch.from_numpy(router).to(dev)
-        layer = EPLayer(DeviceOps(rt, local, E, 2), E, 2, H)
         x = torch.from_numpy(_tokens(rank, T, H)).to(dev)
-        out = layer(x).cpu().numpy()
-        out2 = layer(x).cpu().numpy()
+        if mode == "a2a":
+            layer = EPLayer(DeviceOps(rt, local, E, 2), E, 2, H)
+            out = layer(x).cpu().numpy()
+            out2 = layer(x).cpu().numpy()
+        else:                          # all-gather form, eager and as a captured CUDA graph
+            from distributedmoellm_b200.ep import EPGatherLayer
+            layer = EPGatherLayer(rt, local, E, 2)
+            out = layer(x).clone().cpu().numpy()
+            g = layer.capture(x)
+            g.replay()
+            torch.cuda.synchronize()
+            out2 = layer.buffers(T).out.cpu().numpy()
+            assert layer.status(T) == 0
+            del g
         ref = None
         if rank == 0:                  # the whole layer on one GPU over every rank's tokens
             full = LayerExperts(E, H, I, 32, L.FMT_Q4_F16, L.FMT_Q4_F16, dev)
@@ -77,9 +88,10 @@ def _worker(rank, world, port, q, E, H, I, T):
         q.put((rank, "exception", repr(exc)))
 
 
-@pytest.mark.parametrize("E,H,I,T,tol", [(8, 256, 256, 24, 1e-5), (8, 512, 256, 512, 2e-3)],
-                         ids=["decode", "grouped_gemm"])
-def test_ep_two_gpus_match_one_gpu(E, H, I, T, tol):
+@pytest.mark.parametrize("mode,E,H,I,T,tol", [("a2a", 8, 256, 256, 24, 1e-5), ("a2a", 8, 512, 256, 512, 2e-3),
+                                                ("gather", 8, 256, 256, 24, 1e-5)],
+                         ids=["decode", "grouped_gemm", "gather_decode"])
+def test_ep_two_gpus_match_one_gpu(mode, E, H, I, T, tol):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -87,7 +99,7 @@ def test_ep_two_gpus_match_one_gpu(E, H, I, T, tol):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, E, H, I, T)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, E, H, I, T, mode)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
@@ -108,4 +120,4 @@ def test_ep_two_gpus_match_one_gpu(E, H, I, T, tol):
         want = ref[r * T:(r + 1) * T]
         err = float((np.abs(out - want).max(axis=1) / np.abs(want).max(axis=1)).max())
         assert err < tol, (r, err)
-        assert np.array_equal(out, out2)
+        assert np.array_equal(out, out2)      # repeat (a2a) / graph replay (gather) is bit-identical
