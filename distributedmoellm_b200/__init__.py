@@ -6,7 +6,9 @@ and bound with ctypes) for:
 * bit-exact dequantisation of int4 / int8 / GGUF expert weights;
 * the router (logits, softmax top-k), the stable permute by expert and the
   weighted combine;
-* fused decode mat-vecs over packed experts (gate|up, SiLU, down).
+* fused decode mat-vecs over packed experts (gate|up, SiLU, down);
+* grouped GEMMs on the tcgen05 tensor cores for prefill-sized batches;
+* expert parallelism over NCCL (ep.py).
 
 ``install()`` swaps them in behind moelan's own entry points (its kernels
 module and its ``--gpu`` expert tier), so moelan's coordinator and workers
@@ -23,3 +25,9 @@ def install(moelan_module=None):
     """Patch moelan's expert-compute entry points with the B200 path."""
     from .install import install as _install
     return _install(moelan_module)
+
+
+def uninstall(saved):
+    """Undo :func:`install` (``saved``: what it returned)."""
+    from .install import uninstall as _uninstall
+    return _uninstall(saved)
