@@ -97,12 +97,35 @@ def int8_layer(router, dev, seed=3):
 PREFILL_FLOPS_PER_TOKEN = 2 * K_TOP * 3 * H * I      # 75.5 MFLOP
 
 
+def gguf_layer(dev, seed=4):
+    """Config 4: Mixtral-8x7B MoE layer shape (d_model 4096, 8 experts top-2,
+    intermediate 14336) with GGUF experts: gate and up Q4_K, down Q8_0, the
+    f16 block scales pinned to 0.001 as the reference's random GGUF experts
+    do (128.45 MB per expert)."""
+    import types
+    import torch
+    from distributedmoellm_b200 import layout as L
+    from distributedmoellm_b200 import synthetic as S
+    from distributedmoellm_b200.layer import MoELayer
+    from distributedmoellm_b200.store import LayerExperts
+    NS = types.SimpleNamespace
+    Hm, Im, Em = 4096, 14336, 8
+    rng = np.random.default_rng(seed)
+    ex = LayerExperts(Em, Hm, Im, 32, L.FMT_Q4K_F32, L.FMT_Q8_F16, dev)
+    for e in range(Em):
+        g, u, d = S.gguf_rows(rng, Im, Hm, 12), S.gguf_rows(rng, Im, Hm, 12), S.gguf_rows(rng, Hm, Im, 8)
+        ex.put_expert(e, NS(gu=NS(parts=(NS(raw=g, qtype=12, shape=(Im, Hm)), NS(raw=u, qtype=12, shape=(Im, Hm)))),
+                            down=NS(raw=d, qtype=8, shape=(Hm, Im)), inter=Im))
+    ex.publish()
+    return MoELayer(torch.from_numpy(S.router(rng, Em, Hm)).to(dev), ex, 2, True)
+
+
 def measure_prefill(layer, T, steps, warmup, world, dev, seed=5):
     """Graph replays of the whole layer and of its expert kernels alone at T
     tokens (weights > L2, so every step streams them from HBM)."""
     import torch
     import torch.distributed as dist
-    x = torch.from_numpy(np.random.default_rng(seed).standard_normal((T, H), dtype=np.float32)).to(dev)
+    x = torch.from_numpy(np.random.default_rng(seed).standard_normal((T, layer.H), dtype=np.float32)).to(dev)
     full = layer.capture(x)
     ex = layer.capture(x, experts_only=True)
     torch.cuda.synchronize()
@@ -431,6 +454,25 @@ def run_gpu(args, rank, world, dev):
                                           "kernel": "expert kernels (gather + gate|up GEMM + down GEMM)"}}
             status = max(status, st)
         del l8
+        # config 4: Mixtral-shaped GGUF experts (Q4_K gate/up, Q8_0 down), 1 and 512 tokens
+        lg = gguf_layer(dev)
+        bytes_per_expert = 2 * (14336 * 4096 // 256 * 144) + 4096 * (14336 // 32 * 34)
+        for Tp in (1, 512):
+            m, em, st, gemm = measure_prefill(lg, Tp, max(10, args.steps // 8), 3, world, dev)
+            m, em = max_over_ranks(m), max_over_ranks(em)
+            fl = Tp * 2 * 2 * 3 * 4096 * 14336
+            used = min(8, 2 * Tp)
+            ent = {"tokens_per_s": round(world * Tp / (m / 1e3), 1), "ms_per_step": round(m, 5),
+                   "experts_ms": round(em, 5), "grouped_gemm": True,
+                   "tflops": round(fl / (em / 1e3) / 1e12, 1),
+                   "hbm_gbs": round(used * bytes_per_expert / (em / 1e3) / 1e9, 1)}
+            ent["roofline"] = ({"bound": "hbm", "achieved": ent["hbm_gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                "frac": round(ent["hbm_gbs"] / pk["hbm_gbs"], 4)} if Tp == 1 else
+                               {"bound": "tensor", "achieved": ent["tflops"], "peak": tf_peak, "unit": "TFLOP/s",
+                                "frac": round(ent["tflops"] / tf_peak, 4)})
+            prefill[f"gguf_mixtral_T{Tp}"] = ent
+            status = max(status, st)
+        del lg
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

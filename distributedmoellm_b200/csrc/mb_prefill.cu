@@ -247,6 +247,14 @@ struct Items {
     }
 };
 
+// An f16 pair of exact small integers times the group scale pair, plus the
+// group bias pair for the affine int4 format (one rounding either way).
+template <bool AFF>
+__device__ __forceinline__ uint32_t scale_pair(uint32_t q, uint32_t s, uint32_t b)
+{
+    return AFF ? mb_hfma2(q, s, b) : mb_hmul2(q, s);
+}
+
 // v[t] = the loaded v[(t - rot) & 3]: undoes a load order rotated by rot.
 __device__ __forceinline__ void rotate_back(uint4 (&v)[4], int rot)
 {
@@ -266,6 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 {
     constexpr bool Q8 = (FMT == MB_FMT_Q8_F16 || FMT == MB_FMT_Q8_F32);
     constexpr bool F16S = (FMT == MB_FMT_Q4_F16 || FMT == MB_FMT_Q8_F16);
+    constexpr bool AFF = (FMT == MB_FMT_Q4K_F32);   // int4 with a per-group bias after the scales
     constexpr int kData = Q8 ? 2048 : 1024;
     constexpr int kPStages = pstages(Q8);
 
@@ -462,7 +471,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                         s2[2] = pack_f16(sv.z * wscale, sv.z * wscale);
                         s2[3] = pack_f16(sv.w * wscale, sv.w * wscale);
                     }
-                    if (!ok || !row_ok) s2[0] = s2[1] = s2[2] = s2[3] = 0u;
+                    uint32_t b2[4] = {0u, 0u, 0u, 0u};   // per-group bias (affine int4), times 2^wexp
+                    if (AFF) {
+                        const float4 bv = *reinterpret_cast<const float4*>(blk + kData + 256 + trow * 16);
+                        b2[0] = pack_f16(bv.x * wscale, bv.x * wscale);
+                        b2[1] = pack_f16(bv.y * wscale, bv.y * wscale);
+                        b2[2] = pack_f16(bv.z * wscale, bv.z * wscale);
+                        b2[3] = pack_f16(bv.w * wscale, bv.w * wscale);
+                    }
+                    if (!ok || !row_ok) s2[0] = s2[1] = s2[2] = s2[3] = b2[0] = b2[1] = b2[2] = b2[3] = 0u;
                     // half hh covers groups 2hh, 2hh+1; TMEM column 32*hh + 16*gl + 4*t + i of the slot holds
                     // the f16 pair (column 8t+i, column 8t+i+4) of group 2hh+gl.
                     // A row's four 16-byte lane words are read starting at word rot = (trow >> 1) & 3 (so the
@@ -486,18 +503,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                                 for (int gl = 0; gl < 2; ++gl) {
                                     const uint32_t wd = gl ? wv.y : wv.x, w8 = wd >> 8;
-                                    const uint32_t sg = s2[2 * hh + gl];
+                                    const uint32_t sg = s2[2 * hh + gl], bg = b2[2 * hh + gl];
                                     uint32_t* o = v + 16 * gl + 4 * t;
-                                    o[0] = mb_hmul2(mb_hsub2(mb_lop_and_or(wd, 0x000F000Fu, 0x64006400u), 0x64086408u),
-                                                    sg);
-                                    o[1] = mb_hmul2(
+                                    // (u - 8) * scale (+ bias for the affine format), each pair exact until then
+                                    o[0] = scale_pair<AFF>(
+                                        mb_hsub2(mb_lop_and_or(wd, 0x000F000Fu, 0x64006400u), 0x64086408u), sg, bg);
+                                    o[1] = scale_pair<AFF>(
                                         mb_hfma2(mb_lop_and_or(wd, 0x00F000F0u, 0x64006400u), 0x2C002C00u, 0xD480D480u),
-                                        sg);
-                                    o[2] = mb_hmul2(mb_hsub2(mb_lop_and_or(w8, 0x000F000Fu, 0x64006400u), 0x64086408u),
-                                                    sg);
-                                    o[3] = mb_hmul2(
+                                        sg, bg);
+                                    o[2] = scale_pair<AFF>(
+                                        mb_hsub2(mb_lop_and_or(w8, 0x000F000Fu, 0x64006400u), 0x64086408u), sg, bg);
+                                    o[3] = scale_pair<AFF>(
                                         mb_hfma2(mb_lop_and_or(w8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, 0xD480D480u),
-                                        sg);
+                                        sg, bg);
                                 }
                             }
                         } else {
@@ -685,6 +703,7 @@ int f16_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols)
 
 int block_bytes_of(int fmt)
 {
+    if (fmt == MB_FMT_Q4K_F32) return 1024 + 256 + 256;
     const bool q8 = fmt == MB_FMT_Q8_F16 || fmt == MB_FMT_Q8_F32;
     const bool f16 = fmt == MB_FMT_Q4_F16 || fmt == MB_FMT_Q8_F16;
     return (q8 ? 2048 : 1024) + 64 * (f16 ? 2 : 4);
@@ -723,6 +742,7 @@ int dispatch(int fmt, const PrefillArgs& a, const CUtensorMap& map, cudaStream_t
     case MB_FMT_Q4_F16: return launch<MB_FMT_Q4_F16>(a, map, st);
     case MB_FMT_Q8_F32: return launch<MB_FMT_Q8_F32>(a, map, st);
     case MB_FMT_Q8_F16: return launch<MB_FMT_Q8_F16>(a, map, st);
+    case MB_FMT_Q4K_F32: return launch<MB_FMT_Q4K_F32>(a, map, st);
     default: return mb_fail(MB_EUNSUPPORTED, "mb_moe_prefill: weight format %d", fmt);
     }
 }

@@ -26,6 +26,13 @@ def uses_gemm(experts: LayerExperts, P: int, gemm_min_rows: int) -> bool:
             and P <= 65535 and not experts.missing_exp)
 
 
+def gemm_only(experts) -> bool:
+    """Experts the decode kernels cannot take (the affine int4 format of GGUF
+    Q4_K, or K > 2048 in either matrix) run as grouped GEMMs at any batch size."""
+    from .layout import FMT_Q4K_F32
+    return (FMT_Q4K_F32 in (experts.fmt_gu, experts.fmt_down) or experts.H > 2048 or experts.I > 2048)
+
+
 def run_experts(experts: LayerExperts, x: torch.Tensor, row_exp: torch.Tensor, routing, y: torch.Tensor,
                 workspace, status: torch.Tensor, gemm_min_rows: int, picks: int | None = None) -> None:
     """Every expert's picks through its gate|up, SiLU, down into y (one row
@@ -36,7 +43,11 @@ def run_experts(experts: LayerExperts, x: torch.Tensor, row_exp: torch.Tensor, r
     the picks these experts get (default routing.P; smaller when routing
     covers other ranks' experts too), for the choice of kernels."""
     ex, P = experts, routing.P
-    if uses_gemm(ex, P if picks is None else picks, gemm_min_rows):
+    if gemm_only(ex):
+        # the decode kernels take K <= 2048 and no affine format: every expert as a grouped GEMM
+        D.moe_prefill(ex.table, ex.eexp, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing, y,
+                      workspace("prefill", D.prefill_workspace_bytes(P, ex.H, ex.I)), min_rows=1, status=status)
+    elif uses_gemm(ex, P if picks is None else picks, gemm_min_rows):
         D.moe_decode(ex.table, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing, y,
                      workspace("decode", D.decode_workspace_bytes(P, ex.I)), max_rows=gemm_min_rows - 1,
                      status=status)

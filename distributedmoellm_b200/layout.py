@@ -19,6 +19,9 @@ re-arranged copy, made once when an expert is uploaded:
 * each block is followed by its scales: [16 rows][4 groups] in f16 or f32
   (one per group of 32 columns; a group size of 64 or more repeats its scale);
 * padding rows and columns hold zero weights and zero scales;
+* an affine int4 block (GGUF Q4_K, value = (u - 8) * scale + bias per group
+  of 32) is the int4 block followed by [16 rows][4 groups] f32 biases
+  (1536 bytes);
 * a gate|up matrix (2I rows) interleaves its halves: tile i holds gate rows
   8i..8i+7 and then up rows 8i..8i+7, so one tile yields SiLU(gate) * up.
 
@@ -30,7 +33,7 @@ from __future__ import annotations
 
 import numpy as np
 
-FMT_Q4_F32, FMT_Q4_F16, FMT_Q8_F32, FMT_Q8_F16 = 1, 2, 3, 4
+FMT_Q4_F32, FMT_Q4_F16, FMT_Q8_F32, FMT_Q8_F16, FMT_Q4K_F32 = 1, 2, 3, 4, 5
 TILE_ROWS, QUAD_COLS = 16, 128
 
 
@@ -43,6 +46,8 @@ def scale_is_f16(fmt: int) -> bool:
 
 
 def block_bytes(fmt: int) -> int:
+    if fmt == FMT_Q4K_F32:
+        return 1024 + 64 * 4 + 64 * 4
     return (2048 if is_q8(fmt) else 1024) + 64 * (2 if scale_is_f16(fmt) else 4)
 
 
@@ -150,6 +155,15 @@ def q8_0_as_q8(raw: np.ndarray, cols: int):
     return q, d
 
 
+def exponent_for(amax: float) -> int:
+    """The power-of-two exponent e with amax * 2^e in [2^13, 2^14) (0 for
+    zero or non-finite amax)."""
+    if not (0.0 < amax < 3.0e38):
+        return 0
+    _, ex = np.frexp(np.float32(amax))
+    return int(min(120, max(-120, 14 - int(ex))))
+
+
 def weight_exponent(s, qmax: int) -> int:
     """The power-of-two exponent e that maps a matrix whose weights are at
     most qmax * max|s| in magnitude into [2^13, 2^14) (0 for an all-zero or
@@ -195,6 +209,61 @@ def act_exponent(gu_row_l1: np.ndarray, inter: int) -> int:
     if not (0.0 < b < 1e300):
         return 0
     return int(min(120, max(-120, -13 - int(np.ceil(np.log2(b))))))
+
+
+def _f16_ref(bits: np.ndarray) -> np.ndarray:
+    """f16 bits to f32 as moelan/kernels.py:244-255 decodes them (exponent 31
+    -> +-inf whatever the payload)."""
+    bits = np.asarray(bits, np.uint16)
+    v = bits.view(np.float16).astype(np.float32)
+    inf = ((bits >> 10) & 0x1F) == 31
+    return np.where(inf, np.where(bits & 0x8000, -np.inf, np.inf), v).astype(np.float32)
+
+
+def q4_k_as_affine(raw: np.ndarray, cols: int):
+    """GGUF Q4_K rows (O, cols/256 * 144) -> (nibbles u (O, cols) uint8,
+    scales (O, cols/32) f32, biases (O, cols/32) f32) with
+    (u - 8) * scale + bias = d*sc*q - dmin*m (moelan/kernels.py:310-336):
+    scale = f32(d) * sc, bias = 8 * scale - f32(dmin) * m, u = q."""
+    raw = np.ascontiguousarray(raw, np.uint8)
+    O, nb = raw.shape[0], cols // 256
+    b = raw.reshape(O, nb, 144)
+    d = _f16_ref(np.ascontiguousarray(b[:, :, 0:2]).view(np.uint16)[..., 0])
+    dmin = _f16_ref(np.ascontiguousarray(b[:, :, 2:4]).view(np.uint16)[..., 0])
+    sb = b[:, :, 4:16].astype(np.int32)
+    sc = np.empty((O, nb, 8), np.int32)
+    mn = np.empty((O, nb, 8), np.int32)
+    sc[..., :4], mn[..., :4] = sb[..., 0:4] & 63, sb[..., 4:8] & 63
+    sc[..., 4:] = (sb[..., 8:12] & 0xF) | ((sb[..., 0:4] >> 6) << 4)
+    mn[..., 4:] = (sb[..., 8:12] >> 4) | ((sb[..., 4:8] >> 6) << 4)
+    qs = b[:, :, 16:144].reshape(O, nb, 4, 32)
+    u = np.stack([qs & 15, qs >> 4], axis=3).reshape(O, cols)      # chunk c: low -> 64c+i, high -> 64c+32+i
+    scale = (d[:, :, None] * sc.astype(np.float32)).astype(np.float32)
+    mins = (dmin[:, :, None] * mn.astype(np.float32)).astype(np.float32)
+    bias = (np.float32(8.0) * scale - mins).astype(np.float32)
+    return u.astype(np.uint8), scale.reshape(O, nb * 8), bias.reshape(O, nb * 8)
+
+
+def q4k_tiles(raw: np.ndarray, cols: int, gu_inter: int = 0):
+    """Tile bytes (FMT_Q4K_F32) of GGUF Q4_K rows; ``gu_inter``: I, for a
+    gate|up matrix (2I rows: gate rows then up rows)."""
+    u, sc, bias = q4_k_as_affine(raw, cols)
+    packed = (u[:, 0::2] | (u[:, 1::2] << 4)).astype(np.uint8)
+    base = q4_tiles(packed, sc, 32, True, gu_inter)
+    order = row_order(raw.shape[0], gu_inter)
+    Kp = (cols + QUAD_COLS - 1) // QUAD_COLS * QUAD_COLS
+    NQ, RT = Kp // QUAD_COLS, len(order) // TILE_ROWS
+    Bs = _group_scales(bias, order, cols, 32, np.float32)
+    bt = np.ascontiguousarray(Bs.reshape(RT, TILE_ROWS, NQ, 4).transpose(0, 2, 1, 3)).view(np.uint8).reshape(RT, NQ, -1)
+    return np.ascontiguousarray(np.concatenate([base.reshape(RT, NQ, -1), bt], axis=2).reshape(-1))
+
+
+def q4k_weight_bound(raw: np.ndarray, cols: int):
+    """(largest possible |weight|, per-row sum of |weight| (float64)) of GGUF Q4_K rows."""
+    u, sc, bias = q4_k_as_affine(raw, cols)
+    amax = float(np.max(8.0 * np.abs(sc.astype(np.float64)) + np.abs(bias.astype(np.float64)))) if sc.size else 0.0
+    w = (u.reshape(u.shape[0], -1, 32).astype(np.float64) - 8.0) * sc[..., None] + bias[..., None]
+    return amax, np.abs(w).sum(axis=(1, 2))
 
 
 def q4_0_as_q4(raw: np.ndarray, cols: int):

@@ -33,8 +33,10 @@ class Packed:
 
 
 def _as_group_matrix(m):
-    """(kind, payload, scales, gs, offset): kind 'q4' (payload: colibri int4
-    bytes) or 'q8' (payload: int8 values), or None when there is no packed form."""
+    """(kind, payload, scales, gs, offset[, biases]): kind 'q4' (payload:
+    colibri int4 bytes), 'q8' (int8 values) or 'q4k' (GGUF Q4_K rows as they
+    are: payload the raw blocks, scales the column count), or None when there
+    is no packed form."""
     if hasattr(m, "raw") and hasattr(m, "s") and hasattr(m, "offset"):           # Packed4
         return "q4", np.asarray(m.raw, np.uint8), np.asarray(m.s), int(m.gs), bool(m.offset)
     if hasattr(m, "q") and hasattr(m, "s"):                                      # GroupQuant
@@ -47,10 +49,21 @@ def _as_group_matrix(m):
         if m.qtype == 2:
             raw, d = layout.q4_0_as_q4(m.raw, cols)
             return "q4", raw, d, 32, True
+        if m.qtype == 12:
+            return "q4k", np.asarray(m.raw, np.uint8), cols, 32, False
         return None
     if hasattr(m, "parts"):                                                      # gguf.Stacked
         parts = [_as_group_matrix(p) for p in m.parts]
-        if any(p is None for p in parts) or len({(p[0], p[2].dtype, p[3], p[4]) for p in parts}) != 1:
+        if any(p is None for p in parts):
+            return None
+        kinds = {p[0] for p in parts}
+        if len(kinds) != 1:
+            return None
+        if kinds == {"q4k"}:
+            if len({p[2] for p in parts}) != 1:
+                return None
+            return "q4k", np.concatenate([p[1] for p in parts]), parts[0][2], 32, False
+        if len({(p[2].dtype, p[3], p[4]) for p in parts}) != 1:
             return None
         k, _, s0, gs, off = parts[0]
         return (k, np.concatenate([p[1] for p in parts]), np.concatenate([p[2] for p in parts]).astype(s0.dtype),
@@ -58,28 +71,33 @@ def _as_group_matrix(m):
     return None
 
 
+def _pack_matrix(mat, inter: int):
+    """(fmt, tiles, weight exponent, per-row |w| sums or None) of one matrix;
+    ``inter`` > 0 for a gate|up matrix."""
+    kind, payload, s, gs, off = mat
+    if kind == "q4":
+        return (layout.fmt_of("q4", s), layout.q4_tiles(payload, s, gs, off, gu_inter=inter),
+                layout.weight_exponent(s, 8), layout.row_l1_q4(payload, s, gs, off) if inter else None)
+    if kind == "q8":
+        return (layout.fmt_of("q8", s), layout.q8_tiles(payload, s, gs, gu_inter=inter),
+                layout.weight_exponent(s, 128), layout.row_l1_q8(payload, s, gs) if inter else None)
+    cols = s
+    amax, l1 = layout.q4k_weight_bound(payload, cols)
+    return layout.FMT_Q4K_F32, layout.q4k_tiles(payload, cols, gu_inter=inter), layout.exponent_for(amax), l1
+
+
 def pack_expert(expert, inter: int | None = None):
     """A moelan Expert (gu, down[, inter]) as a Packed, or None if a matrix
-    has no packed form or the two matrices differ in kind / group size."""
+    has no packed form or the two matrices' group sizes differ.  The two
+    matrices may be of different kinds (GGUF experts: Q4_K gate|up, Q8_0 down)."""
     gu, dn = _as_group_matrix(expert.gu), _as_group_matrix(expert.down)
-    if gu is None or dn is None or gu[0] != dn[0] or gu[3] != dn[3]:
+    if gu is None or dn is None or gu[3] != dn[3]:
         return None
-    kind, gs = gu[0], gu[3]
     I = int(inter if inter is not None else expert.inter)
     H = dn[1].shape[0]
     try:
-        if kind == "q4":
-            if gu[4] != dn[4]:
-                return None
-            gt = layout.q4_tiles(gu[1], gu[2], gs, gu[4], gu_inter=I)
-            dt = layout.q4_tiles(dn[1], dn[2], gs, dn[4])
-            ex = (layout.weight_exponent(gu[2], 8), layout.weight_exponent(dn[2], 8),
-                  layout.act_exponent(layout.row_l1_q4(gu[1], gu[2], gs, gu[4]), I))
-        else:
-            gt = layout.q8_tiles(gu[1], gu[2], gs, gu_inter=I)
-            dt = layout.q8_tiles(dn[1], dn[2], gs)
-            ex = (layout.weight_exponent(gu[2], 128), layout.weight_exponent(dn[2], 128),
-                  layout.act_exponent(layout.row_l1_q8(gu[1], gu[2], gs), I))
+        fg, gt, eg, l1 = _pack_matrix(gu, I)
+        fd, dt, ed, _ = _pack_matrix(dn, 0)
     except ValueError:          # a group size the tile layout does not take
         return None
-    return Packed(layout.fmt_of(kind, gu[2]), layout.fmt_of(kind, dn[2]), gs, H, I, gt, dt, ex)
+    return Packed(fg, fd, gu[3], H, I, gt, dt, (eg, ed, layout.act_exponent(l1, I)))

@@ -88,6 +88,18 @@ class LayerExperts:
                        (layout.weight_exponent(gu_s, 128), layout.weight_exponent(dn_s, 128),
                         layout.act_exponent(layout.row_l1_q8(gu_q, gu_s, self.gs), self.I)))
 
+    def put_expert(self, e: int, expert) -> None:
+        """Expert ``e`` from a moelan Expert object (any format packing.py
+        takes: Packed4, GroupQuant, GGUF Q8_0 / Q4_0 / Q4_K and Stacked)."""
+        from .packing import pack_expert
+        p = pack_expert(expert, self.I)
+        if p is None:
+            raise ValueError(f"expert {e} has no packed form")
+        if (p.fmt_gu, p.fmt_down, p.H, p.I) != (self.fmt_gu, self.fmt_down, self.H, self.I) or p.gs % 32:
+            raise ValueError(f"expert {e} is {(p.fmt_gu, p.fmt_down, p.H, p.I)}, this layer "
+                             f"{(self.fmt_gu, self.fmt_down, self.H, self.I)}")
+        self.put_tiles(e, p.gu_tiles, p.dn_tiles, p.eexp)
+
     def publish(self) -> None:
         """Upload the address table after a batch of puts."""
         self.table.copy_(torch.from_numpy(self._table_host))

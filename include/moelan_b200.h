@@ -36,7 +36,9 @@ enum {
     MB_FMT_Q4_F32 = 1, /* int4, two nibbles per byte, group scales f32 */
     MB_FMT_Q4_F16 = 2, /* int4, group scales f16 */
     MB_FMT_Q8_F32 = 3, /* int8, group scales f32 */
-    MB_FMT_Q8_F16 = 4  /* int8, group scales f16 (also GGUF Q8_0 blocks) */
+    MB_FMT_Q8_F16 = 4, /* int8, group scales f16 (also GGUF Q8_0 blocks) */
+    MB_FMT_Q4K_F32 = 5 /* int4 u with value (u - 8) * scale + bias, f32 scales and biases per group of 32
+                          (GGUF Q4_K: scale = d*sc, bias = 8*scale - dmin*m); mb_moe_prefill only */
 };
 
 const char *mb_last_error(void);

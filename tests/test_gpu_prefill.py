@@ -168,3 +168,52 @@ def test_prefill_repeats_bit_identical(qwen_q8):
     for _ in range(6):
         assert torch.equal(layer(x), first)
     assert layer.status(4096) == 0
+
+
+def _gguf_layer(rng, E, H, I, k):
+    """Mixtral-style GGUF experts: gate and up Q4_K (Stacked), down Q8_0."""
+    import types
+    from distributedmoellm_b200 import layout as L
+    from distributedmoellm_b200 import synthetic as S
+    from distributedmoellm_b200.layer import MoELayer
+    from distributedmoellm_b200.store import LayerExperts
+    NS = types.SimpleNamespace
+    ex = LayerExperts(E, H, I, 32, L.FMT_Q4K_F32, L.FMT_Q8_F16, "cuda")
+    desc = {}
+    for e in range(E):
+        g, u = S.gguf_rows(rng, I, H, 12), S.gguf_rows(rng, I, H, 12)
+        d = S.gguf_rows(rng, H, I, 8)
+        ex.put_expert(e, NS(gu=NS(parts=(NS(raw=g, qtype=12, shape=(I, H)), NS(raw=u, qtype=12, shape=(I, H)))),
+                            down=NS(raw=d, qtype=8, shape=(H, I)), inter=I))
+        desc[e] = ([("gguf", g, 12, H), ("gguf", u, 12, H)], ("gguf", d, 8, I))
+    ex.publish()
+    router = S.router(rng, E, H)
+    return MoELayer(cu(router), ex, k, True), desc
+
+
+def _check_gguf_layer(layer, desc, x, I):
+    out = layer(cu(x)).cpu().numpy()
+    b = layer.buffers(x.shape[0])
+    idx, w = b.idx.cpu().numpy(), b.w.cpu().numpy()
+    ex, off, rows, wts = O.group_by_expert(idx, w)
+    groups = [(ex[i], rows[off[i]:off[i + 1]], wts[off[i]:off[i + 1]]) for i in range(len(ex))]
+    want = O.store_compute(x, groups, desc, I)
+    assert row_err(out, want) < TOL_TC
+    assert layer.status(x.shape[0]) == 0
+
+
+def test_gguf_q4_k_layer_matches_oracle(D):
+    rng = np.random.default_rng(12)
+    layer, desc = _gguf_layer(rng, 4, 512, 256, 2)
+    for T in (1, 24, 300):
+        _check_gguf_layer(layer, desc, rng.standard_normal((T, 512), dtype=np.float32), 256)
+
+
+@pytest.mark.parametrize("T", [1, 16])
+def test_gguf_mixtral_shape_matches_oracle(D, T):
+    """Config 4: d_model 4096, 8 experts top-2, intermediate 14336, Q4_K gate/up, Q8_0 down."""
+    global _MIXTRAL
+    if "_MIXTRAL" not in globals():
+        _MIXTRAL = _gguf_layer(np.random.default_rng(4), 8, 4096, 14336, 2)
+    layer, desc = _MIXTRAL
+    _check_gguf_layer(layer, desc, np.random.default_rng(40 + T).standard_normal((T, 4096), dtype=np.float32), 14336)

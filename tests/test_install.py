@@ -50,15 +50,34 @@ def test_pack_int8_and_gguf_and_stacked():
     assert pack_expert(NS(gu=gu40, down=q40, inter=128)).fmt_down == L.FMT_Q4_F16
 
 
-def test_pack_refuses_dense_and_mixed():
+def test_pack_refuses_dense_and_takes_mixed_kinds():
     rng = np.random.default_rng(2)
     gr, gsc, dr, dsc = S.int4_expert(rng, 256, 128, 32, f16_scales=False)
     dense = NS(w=np.zeros((256, 128), np.float32))
     assert pack_expert(NS(gu=packed4(gr, gsc, 32), down=dense, inter=128)) is None
     gq, gs_, dq, ds = S.int8_expert(rng, 256, 128, 32)
-    assert pack_expert(NS(gu=packed4(gr, gsc, 32), down=NS(q=dq, s=ds, gs=32), inter=128)) is None
-    q4k = NS(raw=S.gguf_rows(rng, 256, 256, 12), qtype=12, shape=(256, 256))
-    assert pack_expert(NS(gu=q4k, down=q4k, inter=128)) is None
+    p = pack_expert(NS(gu=packed4(gr, gsc, 32), down=NS(q=dq, s=ds, gs=32), inter=128))
+    assert (p.fmt_gu, p.fmt_down) == (L.FMT_Q4_F32, L.FMT_Q8_F32)
+    q6k = NS(raw=S.gguf_rows(rng, 256, 256, 14), qtype=14, shape=(256, 256))
+    assert pack_expert(NS(gu=q6k, down=q6k, inter=128)) is None
+
+
+def test_pack_gguf_q4_k_reproduces_the_reference_weights():
+    """Q4_K gate|up (Stacked) with a Q8_0 down, Mixtral-style: the affine
+    int4 tiles hold exactly the reference's dequantised values."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+    rng = np.random.default_rng(3)
+    H, I = 512, 256
+    g = NS(raw=S.gguf_rows(rng, I, H, 12), qtype=12, shape=(I, H))
+    u = NS(raw=S.gguf_rows(rng, I, H, 12), qtype=12, shape=(I, H))
+    d = NS(raw=S.gguf_rows(rng, H, I, 8), qtype=8, shape=(H, I))
+    p = pack_expert(NS(gu=NS(parts=(g, u)), down=d, inter=I))
+    assert (p.fmt_gu, p.fmt_down, p.H, p.I) == (L.FMT_Q4K_F32, L.FMT_Q8_F16, H, I)
+    assert len(p.gu_tiles) == L.tiles_nbytes(L.FMT_Q4K_F32, 2 * I, H, gu_inter=I)
+    nib, sc, bias = L.q4_k_as_affine(g.raw, H)
+    w = ((nib.reshape(I, -1, 32).astype(np.float32) - 8) * sc[..., None] + bias[..., None]).reshape(I, H)
+    assert np.array_equal(w, O.gguf_dequant(g.raw, 12, H))
 
 
 def _fake_moelan():
