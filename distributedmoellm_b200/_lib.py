@@ -34,7 +34,7 @@ SIGNATURES = {
                              _vp, _vp, _i64, _vp, _vp]),
     "mb_moe_decode_noalloc": (_int, [_vp, _int, _int, _int, _int, _int, _int, _vp, _vp, _i64, _vp, _vp, _vp, _i64,
                                      _int, _vp, _vp, _vp]),
-    "mb_moe_prefill_workspace_bytes": (_i64, [_i64, _int, _int]),
+    "mb_moe_prefill_workspace_bytes": (_i64, [_i64, _int, _int, _int]),
     "mb_moe_prefill": (_int, [_vp, _vp, _int, _int, _int, _int, _int, _int, _vp, _vp, _i64, _vp, _vp, _vp, _i64,
                               _int, _vp, _vp, _i64, _vp, _vp]),
     "mb_matmul_t_workspace_bytes": (_i64, [_i64]),

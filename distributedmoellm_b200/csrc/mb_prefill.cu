@@ -85,6 +85,11 @@ struct PrefillArgs {
     __half* act;               // phase 1 output (P, I), K-permuted
     float* y;                  // phase 2 output (P, H)
     unsigned* status;
+    // precise gate|up (affine int4): the weights' f16 rounding (piece 0) or its f16 residual (piece 1), and
+    // the gate and up pre-activations written (accumulate 0) or added (1) to pre (P, 2I) f32 instead of act
+    int piece;
+    float* pre;
+    int accumulate;
 };
 
 // ---- tcgen05 / TMA helpers -------------------------------------------------------
@@ -247,12 +252,23 @@ struct Items {
     }
 };
 
-// An f16 pair of exact small integers times the group scale pair, plus the
-// group bias pair for the affine int4 format (one rounding either way).
+// An f16 pair of exact small integers times the group scale (one rounding).
+// For the affine int4 format q * scale + bias is formed in f32 and rounded to
+// f16 once: a scale and bias rounded to f16 first would put the same error
+// on all 32 weights of a group.
 template <bool AFF>
-__device__ __forceinline__ uint32_t scale_pair(uint32_t q, uint32_t s, uint32_t b)
+__device__ __forceinline__ uint32_t scale_pair(uint32_t q, uint32_t s, float sf, float bf, int piece)
 {
-    return AFF ? mb_hfma2(q, s, b) : mb_hmul2(q, s);
+    if (AFF) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&q));
+        const float w0 = fmaf(f.x, sf, bf), w1 = fmaf(f.y, sf, bf);
+        if (piece) {            // the residual w - f16(w), exact in f32, rounded to f16
+            const float2 h = __half22float2(__floats2half2_rn(w0, w1));
+            return pack_f16(w0 - h.x, w1 - h.y);
+        }
+        return pack_f16(w0, w1);
+    }
+    return mb_hmul2(q, s);
 }
 
 // v[t] = the loaded v[(t - rot) & 3]: undoes a load order rotated by rot.
@@ -471,15 +487,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                         s2[2] = pack_f16(sv.z * wscale, sv.z * wscale);
                         s2[3] = pack_f16(sv.w * wscale, sv.w * wscale);
                     }
-                    uint32_t b2[4] = {0u, 0u, 0u, 0u};   // per-group bias (affine int4), times 2^wexp
-                    if (AFF) {
+                    // affine int4: the scales and biases in f32, times 2^wexp (exact)
+                    float sfl[4] = {0.f, 0.f, 0.f, 0.f}, bfl[4] = {0.f, 0.f, 0.f, 0.f};
+                    if (AFF && ok && row_ok) {
+                        const float4 sv = *reinterpret_cast<const float4*>(blk + kData + trow * 16);
                         const float4 bv = *reinterpret_cast<const float4*>(blk + kData + 256 + trow * 16);
-                        b2[0] = pack_f16(bv.x * wscale, bv.x * wscale);
-                        b2[1] = pack_f16(bv.y * wscale, bv.y * wscale);
-                        b2[2] = pack_f16(bv.z * wscale, bv.z * wscale);
-                        b2[3] = pack_f16(bv.w * wscale, bv.w * wscale);
+                        sfl[0] = sv.x * wscale, sfl[1] = sv.y * wscale, sfl[2] = sv.z * wscale, sfl[3] = sv.w * wscale;
+                        bfl[0] = bv.x * wscale, bfl[1] = bv.y * wscale, bfl[2] = bv.z * wscale, bfl[3] = bv.w * wscale;
                     }
-                    if (!ok || !row_ok) s2[0] = s2[1] = s2[2] = s2[3] = b2[0] = b2[1] = b2[2] = b2[3] = 0u;
+                    if (!ok || !row_ok) s2[0] = s2[1] = s2[2] = s2[3] = 0u;
                     // half hh covers groups 2hh, 2hh+1; TMEM column 32*hh + 16*gl + 4*t + i of the slot holds
                     // the f16 pair (column 8t+i, column 8t+i+4) of group 2hh+gl.
                     // A row's four 16-byte lane words are read starting at word rot = (trow >> 1) & 3 (so the
@@ -503,19 +519,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                                 for (int gl = 0; gl < 2; ++gl) {
                                     const uint32_t wd = gl ? wv.y : wv.x, w8 = wd >> 8;
-                                    const uint32_t sg = s2[2 * hh + gl], bg = b2[2 * hh + gl];
+                                    const uint32_t sg = s2[2 * hh + gl];
+                                    const float sf = sfl[2 * hh + gl], bg = bfl[2 * hh + gl];
                                     uint32_t* o = v + 16 * gl + 4 * t;
                                     // (u - 8) * scale (+ bias for the affine format), each pair exact until then
                                     o[0] = scale_pair<AFF>(
-                                        mb_hsub2(mb_lop_and_or(wd, 0x000F000Fu, 0x64006400u), 0x64086408u), sg, bg);
+                                        mb_hsub2(mb_lop_and_or(wd, 0x000F000Fu, 0x64006400u), 0x64086408u), sg, sf, bg, a.piece);
                                     o[1] = scale_pair<AFF>(
                                         mb_hfma2(mb_lop_and_or(wd, 0x00F000F0u, 0x64006400u), 0x2C002C00u, 0xD480D480u),
-                                        sg, bg);
+                                        sg, sf, bg, a.piece);
                                     o[2] = scale_pair<AFF>(
-                                        mb_hsub2(mb_lop_and_or(w8, 0x000F000Fu, 0x64006400u), 0x64086408u), sg, bg);
+                                        mb_hsub2(mb_lop_and_or(w8, 0x000F000Fu, 0x64006400u), 0x64086408u), sg, sf, bg, a.piece);
                                     o[3] = scale_pair<AFF>(
                                         mb_hfma2(mb_lop_and_or(w8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, 0xD480D480u),
-                                        sg, bg);
+                                        sg, sf, bg, a.piece);
                                 }
                             }
                         } else {
@@ -589,7 +606,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint32_t r[32];
                     tmem_ld32(acol + cb, r);
                     if (!ok) continue;
-                    if (a.phase == 1) {
+                    if (a.phase == 1 && a.pre) {
+                        // precise gate|up: lanes s < 16 hold gate row j, lanes 16 + s the up row j; their true
+                        // values go to pre[pick][j] and pre[pick][I + j], written or added
+                        const int s = lane & 15;
+                        const int j = w.mb * 64 + 16 * q + s;
+                        const int col = (lane >= 16 ? a.O_real : 0) + j;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const int n = cb + i;
+                            if (n < nrows && j < a.O_real) {
+                                float* dst = a.pre + (int64_t)(w.off_e + n0 + n) * (2 * a.O_real) + col;
+                                const float v = __uint_as_float(r[i]) * ts[n] * wunscale;
+                                *dst = a.accumulate ? *dst + v : v;
+                            }
+                        }
+                    } else if (a.phase == 1) {
                         // lanes s < 16 hold gate row j, lanes 16 + s the up row j: per pair of tokens (i, i+1)
                         // the low lane forms token i and the high lane token i+1; then lanes s and s+4 (columns
                         // j, j+4: adjacent in the K order) store one f16 pair.
@@ -649,16 +681,57 @@ __device__ __forceinline__ uint4 pack8_perm(const float4 lo, const float4 hi, fl
 // The picks' tokens in pick order as f16, each row scaled by 2^row_exp[row]
 // (K-permuted): xp[p] = f16(x[sorted_rows[p]] * 2^row_exp[sorted_rows[p]]).
 __global__ void gather_f16_kernel(const float* __restrict__ x, const int32_t* __restrict__ sorted_rows,
-                                  const int32_t* __restrict__ row_exp, int64_t P, int H, __half* __restrict__ xp)
+                                  const int32_t* __restrict__ row_exp, int64_t P, int H, __half* __restrict__ xp,
+                                  __half* __restrict__ xp_lo)
 {
     const int64_t p = blockIdx.y;
     const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
     if (p >= P || c >= H) return;
     const int64_t row = sorted_rows[p];
     const float sc = pow2i(clamp120(row_exp[row]));
-    const float4 lo = *reinterpret_cast<const float4*>(x + row * H + c);
-    const float4 hi = *reinterpret_cast<const float4*>(x + row * H + c + 4);
-    *reinterpret_cast<uint4*>(xp + p * H + c) = pack8_perm(lo, hi, sc);
+    float4 lo = *reinterpret_cast<const float4*>(x + row * H + c);
+    float4 hi = *reinterpret_cast<const float4*>(x + row * H + c + 4);
+    lo.x *= sc, lo.y *= sc, lo.z *= sc, lo.w *= sc, hi.x *= sc, hi.y *= sc, hi.z *= sc, hi.w *= sc;
+    const uint4 h = pack8_perm(lo, hi, 1.0f);
+    *reinterpret_cast<uint4*>(xp + p * H + c) = h;
+    if (xp_lo) {                // the residual pieces x * 2^e - f16(x * 2^e), in the same order
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+        const float2 c2 = __half22float2(*reinterpret_cast<const __half2*>(&h.z));
+        const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&h.w));
+        const float4 rl = make_float4(lo.x - a.x, lo.y - b.x, lo.z - c2.x, lo.w - d.x);
+        const float4 rh = make_float4(hi.x - a.y, hi.y - b.y, hi.z - c2.y, hi.w - d.y);
+        *reinterpret_cast<uint4*>(xp_lo + p * H + c) = pack8_perm(rl, rh, 1.0f);
+    }
+}
+
+// SiLU(gate) * up of each pick from the f32 pre-activations of the precise gate|up path (one warp per pick),
+// scaled by the pick's activation exponent and written as f16 in the K order 0 4 1 5 2 6 3 7.
+__global__ void swiglu_act_kernel(const float* __restrict__ pre, int64_t P, int I, const int32_t* __restrict__ offsets,
+                                  int E, const int32_t* __restrict__ e_exp, const int32_t* __restrict__ sorted_rows,
+                                  const int32_t* __restrict__ row_exp, __half* __restrict__ act)
+{
+    const int64_t p = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (p >= P) return;
+    int lo = 0, hi = E;                       // the expert whose picks [offsets[e], offsets[e+1]) hold p
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (offsets[mid] <= p) lo = mid; else hi = mid;
+    }
+    const float sc = pow2i(clamp120(e_exp[4 * lo + 2] + 2 * row_exp[sorted_rows[p]]));
+    const float* g = pre + p * (2 * (int64_t)I);
+    const float* u = g + I;
+    for (int c = lane * 8; c < I; c += 256) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float gv = g[c + j];
+            v[j] = __fdividef(gv, 1.0f + __expf(-gv)) * u[c + j];
+        }
+        *reinterpret_cast<uint4*>(act + p * I + c) =
+            pack8_perm(make_float4(v[0], v[1], v[2], v[3]), make_float4(v[4], v[5], v[6], v[7]), sc);
+    }
 }
 
 // ---- host side -----------------------------------------------------------------------
@@ -752,10 +825,12 @@ int64_t r1k(int64_t n) { return (n + 1023) / 1024 * 1024; }
 }  // namespace
 
 // Workspace (from its first 1024-byte boundary): the picks' tokens as f16 (P x H) | the activations as f16
-// (P x I) | status word.
-extern "C" int64_t mb_moe_prefill_workspace_bytes(int64_t P, int H, int I)
+// (P x I) | status word | for the precise gate|up path (affine int4): the tokens' f16 residuals (P x H) and
+// the pre-activations (P x 2I) f32.
+extern "C" int64_t mb_moe_prefill_workspace_bytes(int64_t P, int H, int I, int fmt_gu)
 {
-    return 1024 + r1k(P * H * 2) + r1k(P * I * 2) + 256;
+    const int64_t extra = fmt_gu == MB_FMT_Q4K_F32 ? r1k(P * H * 2) + r1k(P * 2 * I * 4) : 0;
+    return 1024 + r1k(P * H * 2) + r1k(P * I * 2) + 256 + extra;
 }
 
 extern "C" int mb_moe_prefill(const MbExpert* table, const int32_t* e_exp, int E, int H, int I, int gs, int fmt_gu,
@@ -773,7 +848,8 @@ extern "C" int mb_moe_prefill(const MbExpert* table, const int32_t* e_exp, int E
     MB_REQUIRE(((uintptr_t)x & 15) == 0 && ((uintptr_t)workspace & 15) == 0,
                "mb_moe_prefill: x and workspace must be 16-byte aligned");
     MB_REQUIRE(P <= 65535, "mb_moe_prefill: P=%lld above 65535", (long long)P);
-    MB_REQUIRE(workspace_bytes >= mb_moe_prefill_workspace_bytes(P, H, I), "mb_moe_prefill: workspace too small");
+    MB_REQUIRE(workspace_bytes >= mb_moe_prefill_workspace_bytes(P, H, I, fmt_gu),
+               "mb_moe_prefill: workspace too small");
     if (P == 0) return MB_OK;
     cudaStream_t st = mb_stream(stream);
     uint8_t* ws = reinterpret_cast<uint8_t*>(((uintptr_t)workspace + 1023) & ~(uintptr_t)1023);
@@ -781,12 +857,18 @@ extern "C" int mb_moe_prefill(const MbExpert* table, const int32_t* e_exp, int E
     ws += r1k(P * H * 2);
     __half* act = reinterpret_cast<__half*>(ws);
     ws += r1k(P * I * 2);
+    unsigned* ws_status = reinterpret_cast<unsigned*>(ws);
+    ws += 256;
+    const bool precise = fmt_gu == MB_FMT_Q4K_F32;
+    __half* xp_lo = precise ? reinterpret_cast<__half*>(ws) : nullptr;
+    float* pre = precise ? reinterpret_cast<float*>(ws + r1k(P * H * 2)) : nullptr;
     if (!status) {
-        status = reinterpret_cast<unsigned*>(ws);
+        status = ws_status;
         cudaMemsetAsync(status, 0, sizeof(unsigned), st);
     }
 
-    gather_f16_kernel<<<dim3((H / 8 + 127) / 128, (unsigned)P), 128, 0, st>>>(x, sorted_rows, row_exp, P, H, xp);
+    gather_f16_kernel<<<dim3((H / 8 + 127) / 128, (unsigned)P), 128, 0, st>>>(x, sorted_rows, row_exp, P, H, xp,
+                                                                            xp_lo);
     int rc = mb_check_launch("mb_moe_prefill gather");
     if (rc) return rc;
 
@@ -814,8 +896,30 @@ extern "C" int mb_moe_prefill(const MbExpert* table, const int32_t* e_exp, int E
     a.MB = (a.RT + 7) / 8;
     a.block_bytes = block_bytes_of(fmt_gu);
     a.O_real = I;
-    rc = dispatch(fmt_gu, a, map, st);
-    if (rc) return rc;
+    if (!precise) {
+        rc = dispatch(fmt_gu, a, map, st);
+        if (rc) return rc;
+    } else {
+        // three products with f16 operands, each exact in its f32 accumulation: W_hi x_hi + W_hi x_lo + W_lo x_hi
+        // (W_lo x_lo is below f32 rounding of the sum), then SiLU(gate) * up from the f32 sums
+        CUtensorMap map_lo;
+        rc = f16_map(&map_lo, xp_lo, P, H);
+        if (rc) return rc;
+        a.pre = pre;
+        const CUtensorMap* maps[3] = {&map, &map_lo, &map};
+        for (int pass = 0; pass < 3; ++pass) {
+            a.piece = pass == 2 ? 1 : 0;
+            a.accumulate = pass > 0;
+            rc = dispatch(fmt_gu, a, *maps[pass], st);
+            if (rc) return rc;
+        }
+        a.pre = nullptr;
+        a.piece = a.accumulate = 0;
+        swiglu_act_kernel<<<(unsigned)((P + 7) / 8), 256, 0, st>>>(pre, P, I, offsets, E, e_exp, sorted_rows,
+                                                                   row_exp, act);
+        rc = mb_check_launch("mb_moe_prefill swiglu");
+        if (rc) return rc;
+    }
 
     // down: K = I, rows H -> y (P, H)
     rc = f16_map(&map, act, P, I);

@@ -189,8 +189,8 @@ def moe_decode(table: torch.Tensor, E: int, H: int, I: int, gs: int, fmt_gu: int
     return y
 
 
-def prefill_workspace_bytes(P: int, H: int, I: int) -> int:
-    return int(lib().mb_moe_prefill_workspace_bytes(P, H, I))
+def prefill_workspace_bytes(P: int, H: int, I: int, fmt_gu: int = 0) -> int:
+    return int(lib().mb_moe_prefill_workspace_bytes(P, H, I, int(fmt_gu)))
 
 
 def moe_prefill(table: torch.Tensor, e_exp: torch.Tensor, E: int, H: int, I: int, gs: int, fmt_gu: int,

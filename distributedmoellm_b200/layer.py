@@ -46,13 +46,13 @@ def run_experts(experts: LayerExperts, x: torch.Tensor, row_exp: torch.Tensor, r
     if gemm_only(ex):
         # the decode kernels take K <= 2048 and no affine format: every expert as a grouped GEMM
         D.moe_prefill(ex.table, ex.eexp, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing, y,
-                      workspace("prefill", D.prefill_workspace_bytes(P, ex.H, ex.I)), min_rows=1, status=status)
+                      workspace("prefill", D.prefill_workspace_bytes(P, ex.H, ex.I, ex.fmt_gu)), min_rows=1, status=status)
     elif uses_gemm(ex, P if picks is None else picks, gemm_min_rows):
         D.moe_decode(ex.table, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing, y,
                      workspace("decode", D.decode_workspace_bytes(P, ex.I)), max_rows=gemm_min_rows - 1,
                      status=status)
         D.moe_prefill(ex.table, ex.eexp, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing, y,
-                      workspace("prefill", D.prefill_workspace_bytes(P, ex.H, ex.I)), min_rows=gemm_min_rows,
+                      workspace("prefill", D.prefill_workspace_bytes(P, ex.H, ex.I, ex.fmt_gu)), min_rows=gemm_min_rows,
                       status=status)
     else:
         D.moe_decode(ex.table, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing, y,

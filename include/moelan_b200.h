@@ -164,8 +164,9 @@ int mb_moe_decode_noalloc(const MbExpert *table, int E, int H, int I, int gs, in
 
 /* ---- prefill: grouped GEMMs on the tensor cores ---------------------------------- */
 
-/* Workspace bytes for mb_moe_prefill with P picks. */
-int64_t mb_moe_prefill_workspace_bytes(int64_t P, int H, int I);
+/* Workspace bytes for mb_moe_prefill with P picks (fmt_gu: the gate|up
+ * format; MB_FMT_Q4K_F32 needs room for its precise gate|up products). */
+int64_t mb_moe_prefill_workspace_bytes(int64_t P, int H, int I, int fmt_gu);
 
 /* One MoE layer's routed experts for experts picked by at least min_rows
  * tokens (prefill), as grouped GEMMs (tcgen05, f16 operands, f32
@@ -182,8 +183,12 @@ int64_t mb_moe_prefill_workspace_bytes(int64_t P, int H, int I);
  * below 2^15 (a = -13 - ceil(log2(L1g * L1u)) with L1g, L1u the largest
  * row sums of |weight| of the gate and up halves does); the fourth entry is
  * unused.  Results agree with the f32 reference within 2e-3 of each output
- * row's largest magnitude.  Needs H % 128 == 0, I % 64 == 0, P <= 65535, x
- * and workspace 16-byte aligned. */
+ * row's largest magnitude.  With fmt_gu MB_FMT_Q4K_F32 (GGUF Q4_K: affine
+ * weights whose activations can be heavy-tailed, where f16 operands alone
+ * exceed that bar) the gate|up GEMM runs as three f16 products of the
+ * weights' and tokens' f16 pieces (hi*hi + hi*lo + lo*hi) summed in f32.
+ * Needs H % 128 == 0, I % 64 == 0, P <= 65535, x and workspace 16-byte
+ * aligned. */
 int mb_moe_prefill(const MbExpert *table, const int32_t *e_exp, int E, int H, int I, int gs, int fmt_gu,
                    int fmt_down, const float *x, const int32_t *row_exp, int64_t T, const int32_t *counts,
                    const int32_t *offsets, const int32_t *sorted_rows, int64_t P, int min_rows, float *y,

@@ -74,7 +74,7 @@ def _run(D, ex, desc, counts, min_rows, seed):
     x = rng.standard_normal((T, H), dtype=np.float32)
     r = D.permute(cu(idx[:, None]), cu(np.ones((T, 1), np.float32)), E)
     y = torch.full((T, H), float("nan"), dtype=torch.float32, device="cuda")
-    ws = torch.empty(D.prefill_workspace_bytes(T, H, I), dtype=torch.uint8, device="cuda")
+    ws = torch.empty(D.prefill_workspace_bytes(T, H, I, ex.fmt_gu), dtype=torch.uint8, device="cuda")
     st = torch.zeros(1, dtype=torch.int32, device="cuda")
     xd = cu(x)
     D.moe_prefill(ex.table, ex.eexp, E, H, I, ex.gs, ex.fmt_gu, ex.fmt_down, xd, D.row_exponents(xd), r, y, ws,
