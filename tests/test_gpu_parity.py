@@ -154,6 +154,32 @@ def test_permute_large_and_skewed(D):
     assert int(r.n_unique.item()) == len(ex)
 
 
+@pytest.mark.parametrize("T,k,E", [(1, 1, 1), (2047, 1, 7), (2048, 1, 3), (2049, 1, 5), (750, 8, 64),
+                                   (3000, 6, 60), (8192, 8, 1024), (65536, 1, 2)])
+def test_permute_sizes(D, T, k, E):
+    """One CTA up to 2048 picks, then one more per 2048 up to a cluster of 8:
+    the chunk edges, the largest E (shared memory) and the largest P."""
+    rng = np.random.default_rng(T + E)
+    idx = rng.integers(0, E, (T, k)).astype(np.int32)
+    if E >= k:
+        idx = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+    w = rng.random((T, k), dtype=np.float32)
+    r = D.permute(cu(idx), cu(w), E)
+    ex, off, rows, wts = O.group_by_expert(idx, w)
+    torch.cuda.synchronize()
+    n = int(r.n_unique.item())
+    assert n == len(ex)
+    assert np.array_equal(r.uexperts[:n].cpu().numpy(), ex)
+    assert np.array_equal(r.uoffsets[:n + 1].cpu().numpy(), off)
+    assert np.array_equal(r.sorted_rows.cpu().numpy()[:T * k], rows)
+    assert np.array_equal(r.sorted_w.cpu().numpy()[:T * k], wts)
+    counts = np.bincount(idx.reshape(-1), minlength=E)
+    assert np.array_equal(r.counts.cpu().numpy(), counts)
+    assert np.array_equal(r.offsets.cpu().numpy(), np.concatenate([[0], np.cumsum(counts)]))
+    inv = r.inv[:T * k].cpu().numpy()
+    assert np.array_equal(r.sorted_rows.cpu().numpy()[inv], np.repeat(np.arange(T), k))
+
+
 def test_combine(D):
     rng = np.random.default_rng(1)
     T, k, H = 37, 3, 256
