@@ -41,6 +41,7 @@ constexpr int kMaxKW = 16;      // MMA warps: one per quad (128 columns) of K, s
 constexpr int kEpiWarps = 2;    // epilogue warps, taking alternate items
 constexpr int kMaxMT = 4;       // row tiles per stage
 constexpr int kRedTile = 128;   // floats of one warp's partial of one tile: [8 input rows][16 rows]
+constexpr int kMaxCachedE = 1024;  // experts whose weight address the kernel keeps in shared memory
 
 struct Fmt {
     int data_bytes;   // per block: 1024 (int4) or 2048 (int8)
@@ -90,6 +91,52 @@ struct DecodeArgs {
 __device__ __forceinline__ int64_t items_of(int n, int max_rows, int RTS)
 {
     return (n > 0 && n <= max_rows) ? (int64_t)((n + 7) >> 3) * RTS : 0;
+}
+
+// Estimated cost of the work, for splitting it over the CTAs: an item of a
+// chunk of at most 4 picks costs kCostOne, of 5..8 picks (both N tiles of the
+// MMAs live) kCostTwo, and the first item of a chunk kCostSwitch more (the
+// chunk's activation rows are gathered from global memory there).  Measured
+// on B200: 0.94 / 1.18 us per two-tile item, ~3 us per chunk switch.
+constexpr int kCostOne = 4, kCostTwo = 5, kCostSwitch = 12;
+
+__device__ __forceinline__ int64_t cost_of(int n, int max_rows, int RTS)
+{
+    if (n <= 0 || n > max_rows) return 0;
+    const int64_t full = (n - 1) >> 3;                // chunks of 8 picks before the last
+    const int last = n - 8 * (int)full;               // picks of the last chunk, 1..8
+    return full * ((int64_t)RTS * kCostTwo + kCostSwitch) + (int64_t)RTS * (last > 4 ? kCostTwo : kCostOne) +
+           kCostSwitch;
+}
+
+// The first item whose start cost is at least c (pre: item prefix, cpre: cost prefix over experts).
+__device__ int64_t item_at_cost(const int64_t* pre, const int64_t* cpre, const int32_t* cnt, int E, int RTS, int64_t c)
+{
+    if (c >= cpre[E]) return pre[E];
+    int lo = 0, hi = E;  // the last expert with cpre[lo] <= c (a non-empty one, since cpre[lo + 1] > c)
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (cpre[mid] <= c) lo = mid;
+        else hi = mid;
+    }
+    const int n = cnt[lo];
+    const int64_t full = (n - 1) >> 3;
+    const int last = n - 8 * (int)full;
+    const int64_t tf = (int64_t)RTS * kCostTwo + kCostSwitch;
+    int64_t rel = c - cpre[lo], j;
+    int cc;
+    if (rel < full * tf) {
+        j = rel / tf;
+        rel -= j * tf;
+        cc = kCostTwo;
+    } else {
+        j = full;
+        rel -= full * tf;
+        cc = last > 4 ? kCostTwo : kCostOne;
+    }
+    // item 0 of a chunk spans [0, kCostSwitch + cc), item k >= 1 starts at kCostSwitch + k * cc
+    const int64_t k = rel == 0 ? 0 : max((int64_t)1, (rel - kCostSwitch + cc - 1) / cc);
+    return pre[lo] + j * RTS + k;
 }
 
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
@@ -164,6 +211,70 @@ struct ItemCursor {
     }
 };
 
+// One row tile of one MMA warp: its QPW blocks (16 rows x 128 columns) of a
+// tile in shared memory against the activation fragments bf, group
+// scales applied in f32, the partial sums stored to rt ([input row][16 rows]).
+// blk0: the warp's first block of the tile.
+// TWO: the second N tile (input rows 4..7) is live.
+template <bool Q8, bool F16S, int QPW, bool TWO>
+__device__ __forceinline__ void tile_mma(const uint8_t* __restrict__ blk0, int nq, const uint32_t (&bf)[QPW][2][4][4],
+                                         float* __restrict__ rt, int t, int g)
+{
+    constexpr int kData = Q8 ? 2048 : 1024;
+    constexpr int kBlock = kData + 16 * 4 * (F16S ? 2 : 4);
+    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [N tile][row g, row g+8] of input row 4nt + t
+#pragma unroll
+    for (int qi = 0; qi < QPW; ++qi) {
+        if (qi < nq) {
+            const uint8_t* wp = blk0 + qi * kBlock + g * 64 + t * 16;
+            const uint8_t* sp = blk0 + qi * kBlock + kData + g * (F16S ? 8 : 16);
+            uint32_t wg[Q8 ? 8 : 4], wh[Q8 ? 8 : 4];
+            {
+                const uint4 a0 = *reinterpret_cast<const uint4*>(wp);
+                const uint4 b0 = *reinterpret_cast<const uint4*>(wp + 8 * 64);
+                wg[0] = a0.x; wg[1] = a0.y; wg[2] = a0.z; wg[3] = a0.w;
+                wh[0] = b0.x; wh[1] = b0.y; wh[2] = b0.z; wh[3] = b0.w;
+            }
+            if (Q8) {
+                const uint4 a1 = *reinterpret_cast<const uint4*>(wp + 1024);
+                const uint4 b1 = *reinterpret_cast<const uint4*>(wp + 1024 + 8 * 64);
+                wg[Q8 ? 4 : 0] = a1.x; wg[Q8 ? 5 : 1] = a1.y; wg[Q8 ? 6 : 2] = a1.z; wg[Q8 ? 7 : 3] = a1.w;
+                wh[Q8 ? 4 : 0] = b1.x; wh[Q8 ? 5 : 1] = b1.y; wh[Q8 ? 6 : 2] = b1.z; wh[Q8 ? 7 : 3] = b1.w;
+            }
+            float sg[4], sh[4];
+            scales4<F16S>(sp, sg);
+            scales4<F16S>(sp + 8 * (F16S ? 8 : 16), sh);
+#pragma unroll
+            for (int gi = 0; gi < 4; ++gi) {
+                uint32_t pg[4], ph_[4];
+                if (Q8) {
+                    unpack_q8(wg[(2 * gi) % (Q8 ? 8 : 4)], wg[(2 * gi + 1) % (Q8 ? 8 : 4)], pg);
+                    unpack_q8(wh[(2 * gi) % (Q8 ? 8 : 4)], wh[(2 * gi + 1) % (Q8 ? 8 : 4)], ph_);
+                } else {
+                    unpack_q4(wg[gi], pg);
+                    unpack_q4(wh[gi], ph_);
+                }
+                float d[4];
+                mb_mma_f16_zero(d, pg[0], ph_[0], pg[1], ph_[1], bf[qi][0][gi][0], bf[qi][0][gi][1]);
+                mb_mma_f16(d, pg[2], ph_[2], pg[3], ph_[3], bf[qi][0][gi][2], bf[qi][0][gi][3]);
+                acc[0][0] = fmaf(d[0] + d[1], sg[gi], acc[0][0]);
+                acc[0][1] = fmaf(d[2] + d[3], sh[gi], acc[0][1]);
+                if (TWO) {
+                    float e[4];
+                    mb_mma_f16_zero(e, pg[0], ph_[0], pg[1], ph_[1], bf[qi][1][gi][0], bf[qi][1][gi][1]);
+                    mb_mma_f16(e, pg[2], ph_[2], pg[3], ph_[3], bf[qi][1][gi][2], bf[qi][1][gi][3]);
+                    acc[1][0] = fmaf(e[0] + e[1], sg[gi], acc[1][0]);
+                    acc[1][1] = fmaf(e[2] + e[3], sh[gi], acc[1][1]);
+                }
+            }
+        }
+    }
+    rt[t * 16 + g] = acc[0][0];
+    rt[t * 16 + g + 8] = acc[0][1];
+    rt[(4 + t) * 16 + g] = acc[1][0];
+    rt[(4 + t) * 16 + g + 8] = acc[1][1];
+}
+
 // Warp roles: [0, KW) MMA warps (warp w owns quads QPW*w .. QPW*w+QPW-1 of K), KW the TMA
 // producer, KW+1 and KW+2 the epilogue (even and odd items).  Shared memory:
 // weight stages | reduction buffers [nred][KW][MT][8][16] | mbarriers | item
@@ -190,26 +301,50 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
     uint64_t* empty = full + S;
     uint64_t* rfull = empty + S;
     uint64_t* rempty = rfull + NR;
-    int64_t* pre = reinterpret_cast<int64_t*>(rempty + NR);  // [E+1]
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(pre + E + 1);
+    int64_t* pre = reinterpret_cast<int64_t*>(rempty + NR);  // [E+1] items before expert e
+    int64_t* cpre = pre + E + 1;                                // [E+1] their cost
+    const uint8_t** wptr_s = reinterpret_cast<const uint8_t**>(cpre + E + 1);  // [E] when E <= kMaxCachedE
+    int32_t* cnt_s = reinterpret_cast<int32_t*>(wptr_s + (E <= kMaxCachedE ? E : 0));  // [E] picks per expert
+    int32_t* off_s = cnt_s + E;                                                          // [E] first pick
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(off_s + E);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
 
-    if (warp == 0) {  // items per expert -> prefix
-        int64_t run = 0;
+    // the routing of every expert (and its weights' address) into shared memory,
+    // all loads in flight together
+    for (int e = tid; e < E; e += blockDim.x) {
+        cnt_s[e] = a.single_n ? (e == 0 ? a.single_n : 0) : a.counts[e];
+        off_s[e] = a.single_n ? 0 : a.offsets[e];
+        if (E <= kMaxCachedE)
+            wptr_s[e] = reinterpret_cast<const uint8_t*>(
+                a.single_w ? a.single_w : (a.phase == 1 ? a.table[e].gu : a.table[e].down));
+    }
+    __syncthreads();
+    if (warp == 0) {  // items and costs per expert -> prefixes
+        int64_t run = 0, crun = 0;
         for (int base = 0; base < E; base += 32) {
             const int e = base + lane;
-            int64_t v = 0;
-            if (e < E) v = items_of(a.single_n ? (e == 0 ? a.single_n : 0) : a.counts[e], a.max_rows, RTS);
-            for (int o = 1; o < 32; o <<= 1) {
-                const int64_t u = __shfl_up_sync(0xffffffffu, v, o);
-                if (lane >= o) v += u;
+            int64_t v = 0, cv = 0;
+            if (e < E) {
+                v = items_of(cnt_s[e], a.max_rows, RTS);
+                cv = cost_of(cnt_s[e], a.max_rows, RTS);
             }
-            if (e < E) pre[e + 1] = run + v;
+            for (int o = 1; o < 32; o <<= 1) {
+                const int64_t u = __shfl_up_sync(0xffffffffu, v, o), cu = __shfl_up_sync(0xffffffffu, cv, o);
+                if (lane >= o) {
+                    v += u;
+                    cv += cu;
+                }
+            }
+            if (e < E) {
+                pre[e + 1] = run + v;
+                cpre[e + 1] = crun + cv;
+            }
             run += __shfl_sync(0xffffffffu, v, 31);
+            crun += __shfl_sync(0xffffffffu, cv, 31);
         }
-        if (lane == 0) pre[0] = 0;
+        if (lane == 0) pre[0] = cpre[0] = 0;
     }
     if (tid == 0) {
         for (int i = 0; i < S; ++i) {
@@ -225,8 +360,10 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
     }
     __syncthreads();
 
-    const int64_t total = pre[E];
-    const int64_t lo = total * blockIdx.x / gridDim.x, hi = total * (blockIdx.x + 1) / gridDim.x;
+    // this CTA's contiguous run of items: an equal share of the estimated cost
+    const int64_t ctotal = cpre[E];
+    const int64_t lo = item_at_cost(pre, cpre, cnt_s, E, RTS, ctotal * blockIdx.x / gridDim.x);
+    const int64_t hi = item_at_cost(pre, cpre, cnt_s, E, RTS, ctotal * (blockIdx.x + 1) / gridDim.x);
     if (lo >= hi) return;
     const int64_t n_items = hi - lo;
     ItemCursor cur;
@@ -243,8 +380,10 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
                 if (it >= S && !mb_mbar_wait(&empty[s], ph ^ 1u, a.status, abort_flag)) break;
                 if (cur.e != we) {
                     we = cur.e;
-                    wbase = reinterpret_cast<const uint8_t*>(
-                        a.single_w ? a.single_w : (a.phase == 1 ? a.table[we].gu : a.table[we].down));
+                    wbase = E <= kMaxCachedE ? wptr_s[we]
+                                             : reinterpret_cast<const uint8_t*>(
+                                                   a.single_w ? a.single_w
+                                                              : (a.phase == 1 ? a.table[we].gu : a.table[we].down));
                 }
                 const int nt = min(MT, RT - cur.sg * MT);
                 const uint32_t bytes = (uint32_t)(nt * tile_bytes);
@@ -281,8 +420,8 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
                 if (a.phase == 1 && ke >= 0) flush();
                 ke = cur.e;
                 kc = cur.c;
-                pbase = (a.single_n ? 0 : a.offsets[ke]) + 8 * kc;
-                nvalid = min(8, (a.single_n ? a.single_n : a.counts[ke]) - 8 * kc);
+                pbase = off_s[ke] + 8 * kc;
+                nvalid = min(8, cnt_s[ke] - 8 * kc);
                 int ex = 0;
                 if (n < nvalid) {
                     if (a.phase == 1) ex = a.row_exp[a.sorted_rows[pbase + n]];
@@ -296,6 +435,7 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
                 const float* rr = red + r * red_buf;
                 for (int mt = 0; mt < nt; ++mt) {
                     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
                     for (int w = 0; w < KW; ++w) {
                         const float4 u = *reinterpret_cast<const float4*>(rr + (w * MT + mt) * kRedTile + n * 16 + 4 * rg);
                         v.x += u.x;
@@ -311,10 +451,10 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
                         if (rg < 2 && n < nvalid) {
                             float4 o;
                             float gg;
-                            gg = v.x * fs; o.x = gg / (1.0f + expf(-gg)) * (ux * fs);
-                            gg = v.y * fs; o.y = gg / (1.0f + expf(-gg)) * (uy * fs);
-                            gg = v.z * fs; o.z = gg / (1.0f + expf(-gg)) * (uz * fs);
-                            gg = v.w * fs; o.w = gg / (1.0f + expf(-gg)) * (uw * fs);
+                            gg = v.x * fs; o.x = __fdividef(gg, 1.0f + __expf(-gg)) * (ux * fs);
+                            gg = v.y * fs; o.y = __fdividef(gg, 1.0f + __expf(-gg)) * (uy * fs);
+                            gg = v.z * fs; o.z = __fdividef(gg, 1.0f + __expf(-gg)) * (uz * fs);
+                            gg = v.w * fs; o.w = __fdividef(gg, 1.0f + __expf(-gg)) * (uw * fs);
                             *reinterpret_cast<float4*>(a.act + (int64_t)(pbase + n) * a.act_ld + 8 * rt + 4 * rg) = o;
                             rmax = fmaxf(rmax, fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w))));
                         }
@@ -363,8 +503,8 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
         if (cur.e != ke || cur.c != kc) {
             ke = cur.e;
             kc = cur.c;
-            const int pbase = (a.single_n ? 0 : a.offsets[ke]) + 8 * kc;
-            const int nvalid = min(8, (a.single_n ? a.single_n : a.counts[ke]) - 8 * kc);
+            const int pbase = off_s[ke] + 8 * kc;
+            const int nvalid = min(8, cnt_s[ke] - 8 * kc);
             two = nvalid > 4;
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt) {
@@ -421,61 +561,22 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
         if (it >= NR) mb_mbar_wait(&rempty[r], rph ^ 1u, a.status, abort_flag);
         const bool ok = mb_mbar_wait(&full[s], ph, a.status, abort_flag);
         float* rb = red + r * red_buf + warp * MT * kRedTile;
-        for (int mt = 0; mt < ntiles; ++mt) {
-            float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [N tile][row g, row g+8] of input row 4nt + t
-            if (ok) {
-#pragma unroll
-                for (int qi = 0; qi < QPW; ++qi) {
-                    if (qi < nq) {
-                        const uint8_t* blk =
-                            stages + (size_t)s * stage_bytes + (size_t)mt * tile_bytes + (size_t)(q0 + qi) * kBlock;
-                        uint32_t wg[Q8 ? 8 : 4], wh[Q8 ? 8 : 4];
-                        {
-                            const uint4 a0 = *reinterpret_cast<const uint4*>(blk + g * 64 + t * 16);
-                            const uint4 b0 = *reinterpret_cast<const uint4*>(blk + (g + 8) * 64 + t * 16);
-                            wg[0] = a0.x; wg[1] = a0.y; wg[2] = a0.z; wg[3] = a0.w;
-                            wh[0] = b0.x; wh[1] = b0.y; wh[2] = b0.z; wh[3] = b0.w;
-                        }
-                        if (Q8) {
-                            const uint4 a1 = *reinterpret_cast<const uint4*>(blk + 1024 + g * 64 + t * 16);
-                            const uint4 b1 = *reinterpret_cast<const uint4*>(blk + 1024 + (g + 8) * 64 + t * 16);
-                            wg[Q8 ? 4 : 0] = a1.x; wg[Q8 ? 5 : 1] = a1.y; wg[Q8 ? 6 : 2] = a1.z; wg[Q8 ? 7 : 3] = a1.w;
-                            wh[Q8 ? 4 : 0] = b1.x; wh[Q8 ? 5 : 1] = b1.y; wh[Q8 ? 6 : 2] = b1.z; wh[Q8 ? 7 : 3] = b1.w;
-                        }
-                        float sg[4], sh[4];
-                        scales4<F16S>(blk + kData + g * (F16S ? 8 : 16), sg);
-                        scales4<F16S>(blk + kData + (g + 8) * (F16S ? 8 : 16), sh);
-#pragma unroll
-                        for (int gi = 0; gi < 4; ++gi) {
-                            uint32_t pg[4], ph_[4];
-                            if (Q8) {
-                                unpack_q8(wg[(2 * gi) % (Q8 ? 8 : 4)], wg[(2 * gi + 1) % (Q8 ? 8 : 4)], pg);
-                                unpack_q8(wh[(2 * gi) % (Q8 ? 8 : 4)], wh[(2 * gi + 1) % (Q8 ? 8 : 4)], ph_);
-                            } else {
-                                unpack_q4(wg[gi], pg);
-                                unpack_q4(wh[gi], ph_);
-                            }
-                            float d[4];
-                            mb_mma_f16_zero(d, pg[0], ph_[0], pg[1], ph_[1], bf[qi][0][gi][0], bf[qi][0][gi][1]);
-                            mb_mma_f16(d, pg[2], ph_[2], pg[3], ph_[3], bf[qi][0][gi][2], bf[qi][0][gi][3]);
-                            acc[0][0] = fmaf(d[0] + d[1], sg[gi], acc[0][0]);
-                            acc[0][1] = fmaf(d[2] + d[3], sh[gi], acc[0][1]);
-                            if (two) {
-                                float e[4];
-                                mb_mma_f16_zero(e, pg[0], ph_[0], pg[1], ph_[1], bf[qi][1][gi][0], bf[qi][1][gi][1]);
-                                mb_mma_f16(e, pg[2], ph_[2], pg[3], ph_[3], bf[qi][1][gi][2], bf[qi][1][gi][3]);
-                                acc[1][0] = fmaf(e[0] + e[1], sg[gi], acc[1][0]);
-                                acc[1][1] = fmaf(e[2] + e[3], sh[gi], acc[1][1]);
-                            }
-                        }
-                    }
-                }
+        if (ok) {
+            const uint8_t* stage = stages + (size_t)s * stage_bytes;
+            if (two) {
+                for (int mt = 0; mt < ntiles; ++mt)
+                    tile_mma<Q8, F16S, QPW, true>(stage + mt * tile_bytes + q0 * kBlock, nq, bf,
+                                                  rb + mt * kRedTile, t, g);
+            } else {
+                for (int mt = 0; mt < ntiles; ++mt)
+                    tile_mma<Q8, F16S, QPW, false>(stage + mt * tile_bytes + q0 * kBlock, nq, bf,
+                                                   rb + mt * kRedTile, t, g);
             }
-            float* rt = rb + mt * kRedTile;  // [input row n][16 rows]
-            rt[t * 16 + g] = acc[0][0];
-            rt[t * 16 + g + 8] = acc[0][1];
-            rt[(4 + t) * 16 + g] = acc[1][0];
-            rt[(4 + t) * 16 + g + 8] = acc[1][1];
+        } else {
+            for (int mt = 0; mt < ntiles; ++mt) {
+                float* rt = rb + mt * kRedTile;
+                rt[t * 16 + g] = rt[t * 16 + g + 8] = rt[(4 + t) * 16 + g] = rt[(4 + t) * 16 + g + 8] = 0.f;
+            }
         }
         __syncwarp();
         if (lane == 0) {
@@ -515,15 +616,18 @@ Cfg plan(int fmt, int K, int E, int RT)
     c.MT = (32 * 1024 + c.tile_bytes / 2) / c.tile_bytes;
     c.MT = c.MT < 1 ? 1 : (c.MT > kMaxMT ? kMaxMT : c.MT);
     if (c.MT > RT) c.MT = RT < 1 ? 1 : RT;
-    c.nred = kEpiWarps;
-    const size_t budget = c.KW <= 8 ? 110 * 1024 : 210 * 1024;
+    // reduction buffers: with many MMA warps each epilogue warp keeps two items in
+    // hand (the MMA warps run further ahead); with few, shared memory goes to stages
+    c.nred = c.KW > 8 ? 2 * kEpiWarps : kEpiWarps;
+    const size_t budget = c.KW <= 8 ? 110 * 1024 : 220 * 1024;
     const size_t red = (size_t)c.nred * c.KW * c.MT * kRedTile * sizeof(float);
-    const size_t fixed = red + (size_t)(E + 1) * sizeof(int64_t) + 64 + 16 * sizeof(uint64_t);
+    const size_t cache = 2 * (size_t)(E + 1) * sizeof(int64_t) + (E <= kMaxCachedE ? (size_t)E * sizeof(void*) : 0) +
+                         2 * (size_t)E * sizeof(int32_t);
+    const size_t fixed = red + cache + 64 + 16 * sizeof(uint64_t);
     const size_t stage = (size_t)c.MT * c.tile_bytes;
     int st = budget > fixed ? (int)((budget - fixed) / stage) : 2;
     c.stages = st < 2 ? 2 : (st > 8 ? 8 : st);
-    c.smem = (size_t)c.stages * stage + red + (size_t)(2 * c.stages + 2 * c.nred) * sizeof(uint64_t) +
-             (size_t)(E + 1) * sizeof(int64_t) + 16;
+    c.smem = (size_t)c.stages * stage + red + (size_t)(2 * c.stages + 2 * c.nred) * sizeof(uint64_t) + cache + 16;
     return c;
 }
 
