@@ -15,8 +15,7 @@ namespace {
 // the slices in slice order (deterministic) before the softmax.  Each of the
 // 16 x 16 threads holds a (TT/16) x (EE/16) block of (token, expert) sums in
 // registers, fed from 32-column chunks of x and the router staged k-major in
-// shared memory; a sum runs over its slice's columns in order.  Large batches
-// take 64 x 64 tiles (4 x 4 per thread), small ones 16 x 16 (more CTAs).
+// shared memory; a sum runs over its slice's columns in order.
 constexpr int kLgK = 256;   // columns per K slice
 constexpr int kLgC = 32;    // columns per staged chunk
 
@@ -93,6 +92,52 @@ __global__ void __launch_bounds__(256) router_partial_kernel(const float* __rest
         for (int o = 1; o < TPR; o <<= 1) xmax = fmaxf(xmax, __shfl_xor_sync(0xffffffffu, xmax, o));
         const int r = threadIdx.x / TPR;
         if (threadIdx.x % TPR == 0 && t0 + r < T) part_max[(int64_t)ks * T + t0 + r] = xmax;
+    }
+}
+
+// Small batches: CTA (16 tokens, 16 experts, K slice) stages the whole slice of
+// both operands in one round trip, token- and expert-major, and each thread
+// forms one sum four columns at a time.
+__global__ void __launch_bounds__(256) router_partial_small_kernel(const float* __restrict__ x,
+                                                                   const float* __restrict__ router, int64_t T,
+                                                                   int H, int E, float* __restrict__ part,
+                                                                   float* __restrict__ part_max)
+{
+    __shared__ __align__(16) float xs[16][kLgK + 4];
+    __shared__ __align__(16) float ws[16][kLgK + 4];
+    const int64_t t0 = (int64_t)blockIdx.x * 16;
+    const int e0 = blockIdx.y * 16, ks = blockIdx.z, k0 = ks * kLgK;
+    const int kn = min(kLgK, H - k0);
+    for (int i = threadIdx.x; i < 16 * (kLgK / 4); i += 256) {
+        const int r = i / (kLgK / 4), c = (i % (kLgK / 4)) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f), u = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t0 + r < T && c < kn) v = *reinterpret_cast<const float4*>(x + (t0 + r) * H + k0 + c);
+        if (e0 + r < E && c < kn) u = *reinterpret_cast<const float4*>(router + (int64_t)(e0 + r) * H + k0 + c);
+        *reinterpret_cast<float4*>(&xs[r][c]) = v;
+        *reinterpret_cast<float4*>(&ws[r][c]) = u;
+    }
+    __syncthreads();
+    const int ti = threadIdx.x >> 4, ej = threadIdx.x & 15;
+    float acc = 0.f;
+#pragma unroll 8
+    for (int c = 0; c < kLgK; c += 4) {
+        const float4 xv = *reinterpret_cast<const float4*>(&xs[ti][c]);
+        const float4 wv = *reinterpret_cast<const float4*>(&ws[ej][c]);
+        acc = fmaf(xv.x, wv.x, acc);
+        acc = fmaf(xv.y, wv.y, acc);
+        acc = fmaf(xv.z, wv.z, acc);
+        acc = fmaf(xv.w, wv.w, acc);
+    }
+    const int64_t t = t0 + ti;
+    if (t < T && e0 + ej < E) part[((int64_t)ks * T + t) * E + e0 + ej] = acc;
+    if (part_max && blockIdx.y == 0) {  // this slice's largest |x| of each token
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        for (int r = warp; r < 16; r += 8) {
+            float m = 0.f;
+            for (int c = lane; c < kLgK; c += 32) m = fmaxf(m, fabsf(xs[r][c]));
+            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if (lane == 0 && t0 + r < T) part_max[(int64_t)ks * T + t0 + r] = m;
+        }
     }
 }
 
@@ -265,6 +310,7 @@ __global__ void __launch_bounds__(kPermWarps * 32) permute_kernel(
         }
 #pragma unroll
         for (int j = 0; j < kPermBatch; ++j) {
+            if (b0 + 32 * j >= hi) break;                 // warp-uniform
             const int64_t i = b0 + 32 * j + lane;
             const bool valid = i < hi;
             const int e = ev[j];
@@ -287,18 +333,27 @@ __global__ void __launch_bounds__(kPermWarps * 32) permute_kernel(
         }
         tot[e] = run;
     }
-    cluster.sync();                                   // every CTA's totals are visible
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        int32_t all = 0, before = 0;
-        for (int c = 0; c < nc; ++c) {
-            const int32_t v = cluster.map_shared_rank(tot, c)[e];
-            all += v;
-            before += c < rank ? v : 0;
+    if (nc > 1) {
+        cluster.sync();                               // every CTA's totals are visible
+        for (int e = threadIdx.x; e < E; e += blockDim.x) {
+            int32_t all = 0, before = 0;
+            for (int c = 0; c < nc; ++c) {
+                const int32_t v = cluster.map_shared_rank(tot, c)[e];
+                all += v;
+                before += c < rank ? v : 0;
+            }
+            gtot[e] = all;
+            bef[e] = before;
         }
-        gtot[e] = all;
-        bef[e] = before;
+        cluster.sync();                               // no CTA reads another's memory after this
+    } else {
+        __syncthreads();
+        for (int e = threadIdx.x; e < E; e += blockDim.x) {
+            gtot[e] = tot[e];
+            bef[e] = 0;
+        }
+        __syncthreads();
     }
-    cluster.sync();                                   // no CTA reads another's memory after this
     {  // exclusive scan of the totals over experts, and the compact list of used experts
         __shared__ int32_t wsum[kPermWarps], wcnt[kPermWarps];
         const int e = threadIdx.x;                    // blockDim.x = 1024 >= E
@@ -365,6 +420,7 @@ __global__ void __launch_bounds__(kPermWarps * 32) permute_kernel(
         }
 #pragma unroll
         for (int j = 0; j < kPermBatch; ++j) {
+            if (b0 + 32 * j >= hi) break;                 // warp-uniform
             const int64_t i = b0 + 32 * j + lane;
             const bool valid = i < hi;
             const int e = ev[j];
@@ -483,7 +539,7 @@ static int launch_partial(const float* x, const float* router, int64_t T, int H,
         router_partial_kernel<64, 64><<<grid, 256, 0, st>>>(x, router, T, H, E, part, part_max);
     } else {
         const dim3 grid((unsigned)((T + 15) / 16), (E + 15) / 16, router_slices(H));
-        router_partial_kernel<16, 16><<<grid, 256, 0, st>>>(x, router, T, H, E, part, part_max);
+        router_partial_small_kernel<<<grid, 256, 0, st>>>(x, router, T, H, E, part, part_max);
     }
     return mb_check_launch("router logits");
 }
@@ -558,6 +614,11 @@ extern "C" int mb_permute(const int32_t* idx, const float* w, int64_t T, int k, 
         if (e != cudaSuccess) return mb_fail(MB_ECUDA, "mb_permute: %s", cudaGetErrorString(e));
     }
     const int nc = (int)std::min<int64_t>(kPermMaxCluster, std::max<int64_t>(1, (P + kPermPerCta - 1) / kPermPerCta));
+    if (nc == 1) {  // one CTA: a plain launch
+        permute_kernel<<<1, kPermWarps * 32, smem, mb_stream(stream)>>>(idx, w, P, k, E, counts, offsets, sorted_rows,
+                                                                        sorted_w, inv, uexperts, uoffsets, n_unique);
+        return mb_check_launch("mb_permute");
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(nc);
     cfg.blockDim = dim3(kPermWarps * 32);
