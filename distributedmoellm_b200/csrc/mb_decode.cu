@@ -42,6 +42,7 @@ constexpr int kEpiWarps = 2;    // epilogue warps, taking alternate items
 constexpr int kMaxMT = 4;       // row tiles per stage
 constexpr int kRedTile = 128;   // floats of one warp's partial of one tile: [8 input rows][16 rows]
 constexpr int kMaxCachedE = 1024;  // experts whose weight address the kernel keeps in shared memory
+constexpr int kMaxCachedP = 1024;  // picks whose token row and exponent the kernel keeps in shared memory
 
 struct Fmt {
     int data_bytes;   // per block: 1024 (int4) or 2048 (int8)
@@ -81,6 +82,8 @@ struct DecodeArgs {
     unsigned* act_max;
     float* y;
     int max_rows;
+    int P;            // picks (rows of act / entries of sorted_rows)
+    int PC;           // picks 0..PC-1 have their row and exponent in shared memory
     unsigned* status;
     // single-matrix mode (mb_matmul_t): one "expert" whose phase-2 matrix is
     // single_w, picked by single_n input rows 0..single_n-1
@@ -306,7 +309,10 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
     const uint8_t** wptr_s = reinterpret_cast<const uint8_t**>(cpre + E + 1);  // [E] when E <= kMaxCachedE
     int32_t* cnt_s = reinterpret_cast<int32_t*>(wptr_s + (E <= kMaxCachedE ? E : 0));  // [E] picks per expert
     int32_t* off_s = cnt_s + E;                                                          // [E] first pick
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(off_s + E);
+    const int PC = a.PC;  // picks cached below
+    int32_t* row_s = off_s + E;                                // [PC] phase 1: token row of pick p
+    int32_t* exp_s = row_s + (a.phase == 1 ? PC : 0);          // [PC] exponent of pick p's input row
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(exp_s + PC);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
@@ -369,6 +375,22 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
     ItemCursor cur;
     cur.start(pre, E, RTS, lo);
 
+    // the picks' rows and exponents, filled by the MMA and epilogue warps while the
+    // producer starts the first weight copies (named barrier 1 excludes the producer)
+    if (PC > 0 && warp != KW) {
+        const int nthr = (KW + kEpiWarps) * 32, i0 = warp < KW ? tid : tid - 32;
+        for (int p = i0; p < PC; p += nthr) {
+            if (a.phase == 1) {
+                const int row = a.sorted_rows[p];
+                row_s[p] = row;
+                exp_s[p] = a.row_exp[row];
+            } else {
+                exp_s[p] = mb_row_exponent(__uint_as_float(a.act_max[p]));
+            }
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+    }
+
     // ------------------------------------------------------------- producer
     if (warp == KW) {
         if (lane == 0) {
@@ -424,7 +446,8 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
                 nvalid = min(8, cnt_s[ke] - 8 * kc);
                 int ex = 0;
                 if (n < nvalid) {
-                    if (a.phase == 1) ex = a.row_exp[a.sorted_rows[pbase + n]];
+                    if (pbase + n < PC) ex = exp_s[pbase + n];
+                    else if (a.phase == 1) ex = a.row_exp[a.sorted_rows[pbase + n]];
                     else ex = mb_row_exponent(__uint_as_float(a.act_max[pbase + n]));
                 }
                 fs = pow2f(-ex);
@@ -516,13 +539,14 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
                 float up = 1.0f;
                 if (valid) {
                     int ex;
+                    const int p = pbase + xr;
                     if (a.phase == 1) {
-                        const int row = a.sorted_rows[pbase + xr];
+                        const int row = p < PC ? row_s[p] : a.sorted_rows[p];
                         src = a.x + (int64_t)row * a.src_ld;
-                        ex = a.row_exp[row];
+                        ex = p < PC ? exp_s[p] : a.row_exp[row];
                     } else {
-                        src = a.act + (int64_t)(pbase + xr) * a.src_ld;
-                        ex = mb_row_exponent(__uint_as_float(a.act_max[pbase + xr]));
+                        src = a.act + (int64_t)p * a.src_ld;
+                        ex = p < PC ? exp_s[p] : mb_row_exponent(__uint_as_float(a.act_max[p]));
                     }
                     up = pow2f(ex);
                 }
@@ -595,7 +619,7 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
 }
 
 struct Cfg {
-    int KW, NQ, QPW, MT, stages, tile_bytes, nred;
+    int KW, NQ, QPW, MT, stages, tile_bytes, nred, pc;
     size_t smem;
 };
 
@@ -605,7 +629,7 @@ struct Cfg {
 
 // Stage = MT row tiles of ~32 KB; as many stages as fit in the shared memory
 // of one CTA per SM (many MMA warps) or of two (few MMA warps: short K).
-Cfg plan(int fmt, int K, int E, int RT)
+Cfg plan(int fmt, int K, int E, int RT, int P, int phase)
 {
     Cfg c;
     const Fmt f = fmt_info(fmt);
@@ -619,15 +643,23 @@ Cfg plan(int fmt, int K, int E, int RT)
     // reduction buffers: with many MMA warps each epilogue warp keeps two items in
     // hand (the MMA warps run further ahead); with few, shared memory goes to stages
     c.nred = c.KW > 8 ? 2 * kEpiWarps : kEpiWarps;
-    const size_t budget = c.KW <= 8 ? 110 * 1024 : 220 * 1024;
+    // one CTA per SM with many MMA warps, two with few (113 KB each leaves the per-CTA reserve)
+    const size_t budget = c.KW <= 8 ? 113 * 1024 : 220 * 1024;
     const size_t red = (size_t)c.nred * c.KW * c.MT * kRedTile * sizeof(float);
     const size_t cache = 2 * (size_t)(E + 1) * sizeof(int64_t) + (E <= kMaxCachedE ? (size_t)E * sizeof(void*) : 0) +
                          2 * (size_t)E * sizeof(int32_t);
-    const size_t fixed = red + cache + 64 + 16 * sizeof(uint64_t);
     const size_t stage = (size_t)c.MT * c.tile_bytes;
-    int st = budget > fixed ? (int)((budget - fixed) / stage) : 2;
-    c.stages = st < 2 ? 2 : (st > 8 ? 8 : st);
-    c.smem = (size_t)c.stages * stage + red + (size_t)(2 * c.stages + 2 * c.nred) * sizeof(uint64_t) + cache + 16;
+    auto stages_for = [&](size_t fixed) {
+        const int st = budget > fixed ? (int)((budget - fixed) / stage) : 2;
+        return st < 2 ? 2 : (st > 8 ? 8 : st);
+    };
+    const size_t fixed = red + cache + 64 + 16 * sizeof(uint64_t);
+    // the picks' rows and exponents go to shared memory only where that costs no weight stage
+    const size_t pcache = P <= kMaxCachedP ? (phase == 1 ? 2 : 1) * (size_t)P * sizeof(int32_t) : 0;
+    c.stages = stages_for(fixed);
+    c.pc = (pcache && stages_for(fixed + pcache) == c.stages) ? P : 0;
+    c.smem = (size_t)c.stages * stage + red + (size_t)(2 * c.stages + 2 * c.nred) * sizeof(uint64_t) + cache +
+             (c.pc ? pcache : 0) + 16;
     return c;
 }
 
@@ -635,7 +667,7 @@ template <int FMT>
 int launch_phase(const DecodeArgs& base, int K, int RT, cudaStream_t st)
 {
     DecodeArgs a = base;
-    const Cfg c = plan(FMT, K, a.E, RT);
+    const Cfg c = plan(FMT, K, a.E, RT, a.P, a.phase);
     if (c.KW * 32 + (1 + kEpiWarps) * 32 > threads_max(c.QPW))
         return mb_fail(MB_EUNSUPPORTED, "mb_moe_decode: K=%d needs %d MMA warps (max %d)", K, c.KW,
                        threads_max(c.QPW) / 32 - 1 - kEpiWarps);
@@ -647,6 +679,7 @@ int launch_phase(const DecodeArgs& base, int K, int RT, cudaStream_t st)
     a.stages = c.stages;
     a.tile_bytes = c.tile_bytes;
     a.nred = c.nred;
+    a.PC = c.pc;
     auto kern = c.QPW == 2 ? moe_decode_kernel<FMT, 2> : moe_decode_kernel<FMT, 1>;
     const int threads = (c.KW + 1 + kEpiWarps) * 32;
     // one-time per (device, kernel, configuration): raise the shared-memory
@@ -744,6 +777,7 @@ extern "C" int mb_matmul_t(const void* w_tiles, int fmt, int O, int K, const flo
     a.status = status ? status : ws_status;
     a.single_w = w_tiles;
     a.single_n = (int)n;
+    a.P = (int)n;
     return dispatch_fmt(fmt, [&](auto f) { return launch_phase<decltype(f)::value>(a, K, (O + 15) / 16, st); });
 }
 
@@ -791,6 +825,7 @@ extern "C" int mb_moe_decode(const MbExpert* table, int E, int H, int I, int gs,
     a.act_max = act_max;
     a.y = y;
     a.max_rows = max_rows;
+    a.P = (int)P;
     a.status = status;
     a.act_ld = I_pad;
     a.y_ld = H;
