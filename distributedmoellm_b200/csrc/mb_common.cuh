@@ -159,6 +159,34 @@ __device__ __forceinline__ void mb_bulk_g2s(void* dst, const void* src, uint32_t
         : "memory");
 }
 
+// L2 policies for the copies above: data read once (weights streamed through
+// the kernel) goes first when L2 needs room; data read again (token or
+// activation rows reused by many tiles) is kept.
+__device__ __forceinline__ uint64_t mb_policy_evict_first()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ uint64_t mb_policy_evict_last()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// mb_bulk_g2s with an L2 policy from mb_policy_*.
+__device__ __forceinline__ void mb_bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                                 uint64_t policy)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+            "r"(mb_smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(mb_smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
 __device__ __forceinline__ void mb_named_barrier(int id, int nthreads)
 {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

@@ -394,6 +394,7 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
     // ------------------------------------------------------------- producer
     if (warp == KW) {
         if (lane == 0) {
+            const uint64_t wpol = mb_policy_evict_first();
             int s = 0;
             uint32_t ph = 0;
             int we = -1;
@@ -410,8 +411,8 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
                 const int nt = min(MT, RT - cur.sg * MT);
                 const uint32_t bytes = (uint32_t)(nt * tile_bytes);
                 mb_mbar_arrive_expect_tx(&full[s], bytes);
-                mb_bulk_g2s(stages + (size_t)s * stage_bytes, wbase + (int64_t)cur.sg * MT * tile_bytes, bytes,
-                            &full[s]);
+                mb_bulk_g2s_hint(stages + (size_t)s * stage_bytes, wbase + (int64_t)cur.sg * MT * tile_bytes, bytes,
+                                 &full[s], wpol);   // weights are read once: the token rows stay in L2
                 if (++s == S) {
                     s = 0;
                     ph ^= 1u;
