@@ -63,8 +63,16 @@ constexpr int kDqWarps = 8;    // warps 4..11: two sets of four (one per TMEM la
 constexpr int kEpiWarps = 4;   // warps 12..15
 constexpr int kThreads = 512;
 constexpr int kBHalf = kMaxN * 128;   // bytes of one half (64 columns) of a token stage
-constexpr int kBoxRows = 32;          // token rows per TMA box (kMaxN is a multiple, so boxes never overrun)
-static_assert(kMaxN % kBoxRows == 0 && kBHalf % 1024 == 0, "token stage layout");
+// Token tiles: one TMA box per 64-column half, from the tensor map whose box is the pass's token count
+// rounded up to kBoxStep rows (one instruction per half instead of one per 32 rows; a box never
+// overruns the kMaxN-row stage).
+constexpr int kBoxStep = 32;
+constexpr int kNumBoxMaps = kMaxN / kBoxStep;   // box heights 32, 64, ..., kMaxN
+static_assert(kMaxN % kBoxStep == 0 && kBHalf % 1024 == 0, "token stage layout");
+
+struct TokenMaps {
+    CUtensorMap m[kNumBoxMaps];   // m[i]: boxes of 64 columns x (i + 1) * kBoxStep rows
+};
 
 struct PrefillArgs {
     const MbExpert* table;
@@ -286,7 +294,7 @@ __device__ __forceinline__ void rotate_back(uint4 (&v)[4], int rot)
 
 template <int FMT>
 __global__ void __launch_bounds__(kThreads, 1)
-    prefill_kernel(const __grid_constant__ PrefillArgs a, const __grid_constant__ CUtensorMap bmap)
+    prefill_kernel(const __grid_constant__ PrefillArgs a, const __grid_constant__ TokenMaps bmaps)
 {
     constexpr bool Q8 = (FMT == MB_FMT_Q8_F16 || FMT == MB_FMT_Q8_F32);
     constexpr bool F16S = (FMT == MB_FMT_Q4_F16 || FMT == MB_FMT_Q8_F16);
@@ -382,7 +390,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int pass = 0; pass < w.passes; ++pass) {
                     const int n0 = pass * kMaxN;
                     const int nrows = min(kMaxN, w.n_e - n0);
-                    const int nbox = (((nrows + 15) & ~15) + kBoxRows - 1) / kBoxRows;   // <= kMaxN / kBoxRows
+                    const int nbox = (((nrows + 15) & ~15) + kBoxStep - 1) / kBoxStep;   // box height / kBoxStep
+                    const CUtensorMap* bmap = &bmaps.m[nbox - 1];
                     for (int qd = 0; qd < quads; ++qd, ++gq) {
                         const int bs = (int)(gq % kBStages);
                         const int nh = min(2, KH - 2 * qd);
@@ -390,11 +399,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                             !mb_mbar_wait_spin(&b_empty[bs], (uint32_t)(((gq / kBStages) - 1) & 1), a.status,
                                                abort_flag))
                             break;
-                        mb_mbar_arrive_expect_tx(&b_full[bs], (uint32_t)(nh * nbox * kBoxRows * 128));
+                        mb_mbar_arrive_expect_tx(&b_full[bs], (uint32_t)(nh * nbox * kBoxStep * 128));
                         for (int hh = 0; hh < nh; ++hh)
-                            for (int i = 0; i < nbox; ++i)
-                                tma_load_2d(bst + ((size_t)(bs * 2 + hh) * kMaxN + i * kBoxRows) * 128, &bmap,
-                                            qd * 128 + hh * 64, w.off_e + n0 + i * kBoxRows, &b_full[bs]);
+                            tma_load_2d(bst + (size_t)(bs * 2 + hh) * kMaxN * 128, bmap, qd * 128 + hh * 64,
+                                        w.off_e + n0, &b_full[bs]);
                     }
                 }
             }
@@ -757,20 +765,23 @@ int encode_fn(EncodeTiledFn* out)
     return MB_OK;
 }
 
-// Tensor map of a (rows, cols) row-major f16 matrix, boxes of 64 columns x kBoxRows rows, 128-byte swizzle.
-int f16_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols)
+// Tensor maps of a (rows, cols) row-major f16 matrix, boxes of 64 columns x 32, 64, ..., kMaxN rows,
+// 128-byte swizzle.
+int f16_maps(TokenMaps* maps, const void* base, int64_t rows, int64_t cols)
 {
     EncodeTiledFn fn;
     int rc = encode_fn(&fn);
     if (rc) return rc;
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    const cuuint32_t box[2] = {64, kBoxRows};
     const cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return mb_fail(MB_ECUDA, "mb_moe_prefill: cuTensorMapEncodeTiled failed (%d)", (int)r);
+    for (int i = 0; i < kNumBoxMaps; ++i) {
+        const cuuint32_t box[2] = {64, (cuuint32_t)((i + 1) * kBoxStep)};
+        CUresult r = fn(&maps->m[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return mb_fail(MB_ECUDA, "mb_moe_prefill: cuTensorMapEncodeTiled failed (%d)", (int)r);
+    }
     return MB_OK;
 }
 
@@ -790,7 +801,7 @@ size_t smem_bytes(int fmt, int block_bytes, int E)
 }
 
 template <int FMT>
-int launch(const PrefillArgs& a, const CUtensorMap& map, cudaStream_t st)
+int launch(const PrefillArgs& a, const TokenMaps& maps, cudaStream_t st)
 {
     auto kern = prefill_kernel<FMT>;
     const size_t smem = smem_bytes(FMT, a.block_bytes, a.E);
@@ -804,11 +815,11 @@ int launch(const PrefillArgs& a, const CUtensorMap& map, cudaStream_t st)
     }
     const int items = a.E * a.MB;
     const int grid = items < mb_num_sms() ? items : mb_num_sms();
-    kern<<<grid, kThreads, smem, st>>>(a, map);
+    kern<<<grid, kThreads, smem, st>>>(a, maps);
     return mb_check_launch("mb_moe_prefill");
 }
 
-int dispatch(int fmt, const PrefillArgs& a, const CUtensorMap& map, cudaStream_t st)
+int dispatch(int fmt, const PrefillArgs& a, const TokenMaps& map, cudaStream_t st)
 {
     switch (fmt) {
     case MB_FMT_Q4_F32: return launch<MB_FMT_Q4_F32>(a, map, st);
@@ -885,9 +896,9 @@ extern "C" int mb_moe_prefill(const MbExpert* table, const int32_t* e_exp, int E
     a.act = act;
     a.y = y;
 
-    CUtensorMap map;
+    TokenMaps map;
     // gate|up: K = H, rows 2I (RT = I/8 tiles of 8 gate + 8 up rows) -> act (P, I) f16
-    rc = f16_map(&map, xp, P, H);
+    rc = f16_maps(&map, xp, P, H);
     if (rc) return rc;
     a.phase = 1;
     a.NQ = H / 128;
@@ -902,11 +913,11 @@ extern "C" int mb_moe_prefill(const MbExpert* table, const int32_t* e_exp, int E
     } else {
         // three products with f16 operands, each exact in its f32 accumulation: W_hi x_hi + W_hi x_lo + W_lo x_hi
         // (W_lo x_lo is below f32 rounding of the sum), then SiLU(gate) * up from the f32 sums
-        CUtensorMap map_lo;
-        rc = f16_map(&map_lo, xp_lo, P, H);
+        TokenMaps map_lo;
+        rc = f16_maps(&map_lo, xp_lo, P, H);
         if (rc) return rc;
         a.pre = pre;
-        const CUtensorMap* maps[3] = {&map, &map_lo, &map};
+        const TokenMaps* maps[3] = {&map, &map_lo, &map};
         for (int pass = 0; pass < 3; ++pass) {
             a.piece = pass == 2 ? 1 : 0;
             a.accumulate = pass > 0;
@@ -922,7 +933,7 @@ extern "C" int mb_moe_prefill(const MbExpert* table, const int32_t* e_exp, int E
     }
 
     // down: K = I, rows H -> y (P, H)
-    rc = f16_map(&map, act, P, I);
+    rc = f16_maps(&map, act, P, I);
     if (rc) return rc;
     a.phase = 2;
     a.NQ = (I + 127) / 128;
