@@ -358,24 +358,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     // gq % kASlots, token stage gq % kBStages, dequant set gq % 2.
     if (warp == 0) {
         // ------------------------------------------------------------ weight producer
-        if (lane == 0) {
+        {
             Items w(a, meta);
             int gq = 0;
-            while (w.next() && !*abort_flag) {
+            bool ok = true;
+            while (ok && w.next() && !*abort_flag) {
                 const int tiles = min(8, a.RT - w.mb * 8);
                 const uint8_t* wbase =
                     reinterpret_cast<const uint8_t*>(a.phase == 1 ? a.table[w.e].gu : a.table[w.e].down);
-                for (int pass = 0; pass < w.passes; ++pass) {
+                for (int pass = 0; ok && pass < w.passes; ++pass) {
                     for (int qd = 0; qd < quads; ++qd, ++gq) {
                         const int ps = (int)(gq % kPStages);
-                        if (gq >= kPStages &&
-                            !mb_mbar_wait_spin(&p_empty[ps], (uint32_t)(((gq / kPStages) - 1) & 1), a.status,
-                                               abort_flag))
-                            break;
-                        mb_mbar_arrive_expect_tx(&p_full[ps], (uint32_t)(tiles * a.block_bytes));
-                        for (int i = 0; i < tiles; ++i)
-                            mb_bulk_g2s(pst + ((size_t)ps * 8 + i) * a.block_bytes,
-                                        wbase + ((size_t)(w.mb * 8 + i) * a.NQ + qd) * a.block_bytes,
+                        if (gq >= kPStages)
+                            ok = __all_sync(0xffffffffu, mb_mbar_wait_spin(&p_empty[ps], (uint32_t)(((gq / kPStages) - 1) & 1),
+                                                                          a.status, abort_flag));
+                        if (!ok) break;
+                        if (lane == 0) mb_mbar_arrive_expect_tx(&p_full[ps], (uint32_t)(tiles * a.block_bytes));
+                        __syncwarp();
+                        if (lane < tiles)   // one lane per row tile: the copies are issued in parallel
+                            mb_bulk_g2s(pst + ((size_t)ps * 8 + lane) * a.block_bytes,
+                                        wbase + ((size_t)(w.mb * 8 + lane) * a.NQ + qd) * a.block_bytes,
                                         (uint32_t)a.block_bytes, &p_full[ps]);
                     }
                 }
@@ -383,11 +385,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ token producer
-        if (lane == 0) {
+        {
             Items w(a, meta);
             int gq = 0;
-            while (w.next() && !*abort_flag) {
-                for (int pass = 0; pass < w.passes; ++pass) {
+            bool ok = true;
+            while (ok && w.next() && !*abort_flag) {
+                for (int pass = 0; ok && pass < w.passes; ++pass) {
                     const int n0 = pass * kMaxN;
                     const int nrows = min(kMaxN, w.n_e - n0);
                     const int nbox = (((nrows + 15) & ~15) + kBoxStep - 1) / kBoxStep;   // box height / kBoxStep
@@ -395,13 +398,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int qd = 0; qd < quads; ++qd, ++gq) {
                         const int bs = (int)(gq % kBStages);
                         const int nh = min(2, KH - 2 * qd);
-                        if (gq >= kBStages &&
-                            !mb_mbar_wait_spin(&b_empty[bs], (uint32_t)(((gq / kBStages) - 1) & 1), a.status,
-                                               abort_flag))
-                            break;
-                        mb_mbar_arrive_expect_tx(&b_full[bs], (uint32_t)(nh * nbox * kBoxStep * 128));
-                        for (int hh = 0; hh < nh; ++hh)
-                            tma_load_2d(bst + (size_t)(bs * 2 + hh) * kMaxN * 128, bmap, qd * 128 + hh * 64,
+                        if (gq >= kBStages)
+                            ok = __all_sync(0xffffffffu, mb_mbar_wait_spin(&b_empty[bs], (uint32_t)(((gq / kBStages) - 1) & 1),
+                                                                          a.status, abort_flag));
+                        if (!ok) break;
+                        if (lane == 0) mb_mbar_arrive_expect_tx(&b_full[bs], (uint32_t)(nh * nbox * kBoxStep * 128));
+                        __syncwarp();
+                        if (lane < nh)   // one lane per 64-column half
+                            tma_load_2d(bst + (size_t)(bs * 2 + lane) * kMaxN * 128, bmap, qd * 128 + lane * 64,
                                         w.off_e + n0, &b_full[bs]);
                     }
                 }
