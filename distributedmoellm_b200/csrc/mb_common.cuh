@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/moelan_b200.h"
 
 // ---- host-side error reporting -------------------------------------------------
@@ -14,6 +16,32 @@ int mb_fail(int code, const char* fmt, ...);
 
 // Returns MB_OK, or records the pending CUDA launch error and returns MB_ECUDA.
 int mb_check_launch(const char* what);
+
+// Programmatic dependent launch.  A kernel launched by mb_launch_pdl may start
+// while the kernel before it in the stream is still running (its CTAs are
+// placed as that kernel's CTAs leave the SMs); it calls mb_pdl_wait() before
+// the first read of anything that kernel wrote, which returns once that kernel
+// has completed and its writes are visible (at once when there is no such
+// kernel).  mb_pdl_trigger() lets the next kernel start launching.
+__device__ __forceinline__ void mb_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void mb_pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t mb_launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                 Args&&... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 #define MB_REQUIRE(cond, ...)                                  \
     do {                                                       \

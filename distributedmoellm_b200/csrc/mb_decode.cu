@@ -317,6 +317,13 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
 
+    // Launched programmatically after the kernel before it (mb_launch_pdl).  The gate|up phase reads the
+    // routing that kernel wrote, so it waits first.  The down phase needs only the routing (complete
+    // before the gate|up phase began) and its own weights until it reads the activations: its producer
+    // starts streaming while the gate|up phase drains, the other warps wait below.
+    if (a.phase == 1) mb_pdl_wait();
+    mb_pdl_trigger();
+
     // the routing of every expert (and its weights' address) into shared memory,
     // all loads in flight together
     for (int e = tid; e < E; e += blockDim.x) {
@@ -377,6 +384,7 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
 
     // the picks' rows and exponents, filled by the MMA and epilogue warps while the
     // producer starts the first weight copies (named barrier 1 excludes the producer)
+    if (a.phase == 2 && warp != KW) mb_pdl_wait();   // the activations and their maxima are complete
     if (PC > 0 && warp != KW) {
         const int nthr = (KW + kEpiWarps) * 32, i0 = warp < KW ? tid : tid - 32;
         for (int p = i0; p < PC; p += nthr) {
@@ -714,8 +722,9 @@ int launch_phase(const DecodeArgs& base, int K, int RT, cudaStream_t st)
         if (ncache < 16) cache[ncache++] = Occ{dev, threads, c.smem, per_sm, c.QPW};
     }
     const int grid = mb_num_sms() * per_sm;
-    kern<<<grid, threads, c.smem, st>>>(a);
-    return mb_check_launch("mb_moe_decode");
+    const cudaError_t le = mb_launch_pdl(kern, dim3(grid), dim3(threads), c.smem, st, a);
+    if (le != cudaSuccess) return mb_fail(MB_ECUDA, "mb_moe_decode launch: %s", cudaGetErrorString(le));
+    return MB_OK;
 }
 
 template <typename F>

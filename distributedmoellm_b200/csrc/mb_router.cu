@@ -32,6 +32,8 @@ __global__ void __launch_bounds__(256) router_partial_kernel(const float* __rest
     static_assert(RE == 1 || RE == 2 || RE == 4, "expert tile");
     __shared__ __align__(16) float xs[kLgC][PT];        // [column][token]
     __shared__ __align__(16) float ws[kLgC][PE];        // [column][expert]
+    mb_pdl_wait();
+    mb_pdl_trigger();
     const int64_t t0 = (int64_t)blockIdx.x * TT;
     const int e0 = blockIdx.y * EE, ks = blockIdx.z, k0 = ks * kLgK;
     const int kn = min(kLgK, H - k0);
@@ -105,6 +107,8 @@ __global__ void __launch_bounds__(256) router_partial_small_kernel(const float* 
 {
     __shared__ __align__(16) float xs[16][kLgK + 4];
     __shared__ __align__(16) float ws[16][kLgK + 4];
+    mb_pdl_wait();
+    mb_pdl_trigger();
     const int64_t t0 = (int64_t)blockIdx.x * 16;
     const int e0 = blockIdx.y * 16, ks = blockIdx.z, k0 = ks * kLgK;
     const int kn = min(kLgK, H - k0);
@@ -169,6 +173,8 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int nslices
                                    float* __restrict__ out_logits, int32_t* __restrict__ row_exp, int64_t T, int E,
                                    int k, int normalize, int32_t* __restrict__ idx, float* __restrict__ w)
 {
+    mb_pdl_wait();
+    mb_pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
     if (t >= T) return;
@@ -284,6 +290,8 @@ __global__ void __launch_bounds__(kPermWarps * 32) permute_kernel(
     int32_t* offsets, int32_t* sorted_rows, float* sorted_w, int32_t* inv, int32_t* uexperts, int32_t* uoffsets,
     int32_t* n_unique)
 {
+    mb_pdl_wait();
+    mb_pdl_trigger();
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
     const int nc = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
@@ -451,6 +459,8 @@ __global__ void combine_kernel(const float* __restrict__ y, const int32_t* __res
                                const int32_t* __restrict__ pair_idx, const float* __restrict__ pair_w, int64_t T,
                                int k, int H, int accumulate, float* __restrict__ out)
 {
+    mb_pdl_wait();
+    mb_pdl_trigger();
     const int64_t r = blockIdx.y;
     const int h = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
     if (h >= H) return;
@@ -485,29 +495,21 @@ __global__ void combine_kernel(const float* __restrict__ y, const int32_t* __res
 
 static int router_slices(int H) { return (H + kLgK - 1) / kLgK; }
 
-static void launch_topk(const float* logits, int nslices, const float* part_max, float* out_logits, int32_t* row_exp,
-                        int64_t T, int E, int k, int normalize, int32_t* idx, float* w, cudaStream_t st)
+static int launch_topk(const float* logits, int nslices, const float* part_max, float* out_logits, int32_t* row_exp,
+                       int64_t T, int E, int k, int normalize, int32_t* idx, float* w, cudaStream_t st)
 {
     const dim3 grid((unsigned)((T + 7) / 8)), block(256);
     const int per = (E + 31) / 32;
-    if (per <= 1)
-        router_topk_kernel<1><<<grid, block, 0, st>>>(logits, nslices, part_max, out_logits, row_exp, T, E, k,
-                                                      normalize, idx, w);
-    else if (per <= 2)
-        router_topk_kernel<2><<<grid, block, 0, st>>>(logits, nslices, part_max, out_logits, row_exp, T, E, k,
-                                                      normalize, idx, w);
-    else if (per <= 4)
-        router_topk_kernel<4><<<grid, block, 0, st>>>(logits, nslices, part_max, out_logits, row_exp, T, E, k,
-                                                      normalize, idx, w);
-    else if (per <= 8)
-        router_topk_kernel<8><<<grid, block, 0, st>>>(logits, nslices, part_max, out_logits, row_exp, T, E, k,
-                                                      normalize, idx, w);
-    else if (per <= 16)
-        router_topk_kernel<16><<<grid, block, 0, st>>>(logits, nslices, part_max, out_logits, row_exp, T, E, k,
-                                                       normalize, idx, w);
-    else
-        router_topk_kernel<32><<<grid, block, 0, st>>>(logits, nslices, part_max, out_logits, row_exp, T, E, k,
-                                                       normalize, idx, w);
+    auto kern = per <= 1 ? router_topk_kernel<1>
+              : per <= 2 ? router_topk_kernel<2>
+              : per <= 4 ? router_topk_kernel<4>
+              : per <= 8 ? router_topk_kernel<8>
+              : per <= 16 ? router_topk_kernel<16>
+                          : router_topk_kernel<32>;
+    const cudaError_t e = mb_launch_pdl(kern, grid, block, 0, st, logits, nslices, part_max, out_logits, row_exp, T,
+                                        E, k, normalize, idx, w);
+    if (e != cudaSuccess) return mb_fail(MB_ECUDA, "router top-k launch: %s", cudaGetErrorString(e));
+    return MB_OK;
 }
 
 __global__ void sum_slices_kernel(const float* __restrict__ part, int nslices, const float* __restrict__ part_max,
@@ -534,14 +536,16 @@ static int launch_partial(const float* x, const float* router, int64_t T, int H,
     MB_REQUIRE(((uintptr_t)x & 15) == 0 && ((uintptr_t)router & 15) == 0, "router logits: x/router not 16-byte aligned");
     MB_REQUIRE((T + 15) / 16 <= 0x7fffffff && (E + 15) / 16 <= 65535, "router logits: too large");
     if (T == 0) return MB_OK;
+    cudaError_t e;
     if (T >= 512) {
         const dim3 grid((unsigned)((T + 63) / 64), (E + 63) / 64, router_slices(H));
-        router_partial_kernel<64, 64><<<grid, 256, 0, st>>>(x, router, T, H, E, part, part_max);
+        e = mb_launch_pdl(router_partial_kernel<64, 64>, grid, dim3(256), 0, st, x, router, T, H, E, part, part_max);
     } else {
         const dim3 grid((unsigned)((T + 15) / 16), (E + 15) / 16, router_slices(H));
-        router_partial_small_kernel<<<grid, 256, 0, st>>>(x, router, T, H, E, part, part_max);
+        e = mb_launch_pdl(router_partial_small_kernel, grid, dim3(256), 0, st, x, router, T, H, E, part, part_max);
     }
-    return mb_check_launch("router logits");
+    if (e != cudaSuccess) return mb_fail(MB_ECUDA, "router logits launch: %s", cudaGetErrorString(e));
+    return MB_OK;
 }
 
 extern "C" int64_t mb_router_workspace_bytes(int64_t T, int H, int E)
@@ -577,7 +581,8 @@ extern "C" int mb_router_route(const float* x, const float* router, int64_t T, i
     float* pmax = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + (((int64_t)ns * T * E * 4 + 255) / 256) * 256);
     int rc = launch_partial(x, router, T, H, E, part, pmax, mb_stream(stream));
     if (rc || T == 0) return rc;
-    launch_topk(part, ns, pmax, logits, row_exp, T, E, k, normalize, idx, w, mb_stream(stream));
+    rc = launch_topk(part, ns, pmax, logits, row_exp, T, E, k, normalize, idx, w, mb_stream(stream));
+    if (rc) return rc;
     return mb_check_launch("mb_router_route");
 }
 
@@ -596,7 +601,8 @@ extern "C" int mb_router_topk(const float* logits, int64_t T, int E, int k, int 
     MB_REQUIRE(E > 0 && E <= 32 * kTopkMaxPerLane, "mb_router_topk: E=%d outside 1..1024", E);
     MB_REQUIRE(k > 0 && k <= E && k <= 32, "mb_router_topk: k=%d outside 1..min(E,32)", k);
     if (T == 0) return MB_OK;
-    launch_topk(logits, 0, nullptr, nullptr, nullptr, T, E, k, normalize, idx, w, mb_stream(stream));
+    const int rc = launch_topk(logits, 0, nullptr, nullptr, nullptr, T, E, k, normalize, idx, w, mb_stream(stream));
+    if (rc) return rc;
     return mb_check_launch("mb_router_topk");
 }
 
@@ -614,23 +620,27 @@ extern "C" int mb_permute(const int32_t* idx, const float* w, int64_t T, int k, 
         if (e != cudaSuccess) return mb_fail(MB_ECUDA, "mb_permute: %s", cudaGetErrorString(e));
     }
     const int nc = (int)std::min<int64_t>(kPermMaxCluster, std::max<int64_t>(1, (P + kPermPerCta - 1) / kPermPerCta));
-    if (nc == 1) {  // one CTA: a plain launch
-        permute_kernel<<<1, kPermWarps * 32, smem, mb_stream(stream)>>>(idx, w, P, k, E, counts, offsets, sorted_rows,
-                                                                        sorted_w, inv, uexperts, uoffsets, n_unique);
-        return mb_check_launch("mb_permute");
+    if (nc == 1) {  // one CTA: no cluster
+        const cudaError_t e = mb_launch_pdl(permute_kernel, dim3(1), dim3(kPermWarps * 32), smem, mb_stream(stream), idx,
+                                            w, P, k, E, counts, offsets, sorted_rows, sorted_w, inv, uexperts,
+                                            uoffsets, n_unique);
+        if (e != cudaSuccess) return mb_fail(MB_ECUDA, "mb_permute launch: %s", cudaGetErrorString(e));
+        return MB_OK;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(nc);
     cfg.blockDim = dim3(kPermWarps * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = mb_stream(stream);
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = nc;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // see mb_launch_pdl
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     cudaError_t le = cudaLaunchKernelEx(&cfg, permute_kernel, idx, w, P, k, E, counts, offsets, sorted_rows, sorted_w,
                                         inv, uexperts, uoffsets, n_unique);
     if (le != cudaSuccess) return mb_fail(MB_ECUDA, "mb_permute launch: %s", cudaGetErrorString(le));
@@ -647,6 +657,8 @@ extern "C" int mb_unpermute_combine(const float* y, const int32_t* row_ptr, cons
     MB_REQUIRE(T <= 65535, "mb_unpermute_combine: T=%lld above 65535", (long long)T);
     if (T == 0) return MB_OK;
     dim3 grid((H / 4 + 255) / 256, (unsigned)T);
-    combine_kernel<<<grid, 256, 0, mb_stream(stream)>>>(y, row_ptr, pair_idx, pair_w, T, k, H, accumulate, out);
+    const cudaError_t e = mb_launch_pdl(combine_kernel, grid, dim3(256), 0, mb_stream(stream), y, row_ptr, pair_idx,
+                                        pair_w, T, k, H, accumulate, out);
+    if (e != cudaSuccess) return mb_fail(MB_ECUDA, "mb_unpermute_combine launch: %s", cudaGetErrorString(e));
     return mb_check_launch("mb_unpermute_combine");
 }
