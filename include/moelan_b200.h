@@ -10,6 +10,12 @@
  * whose size the *_workspace_bytes functions return.  Buffers are owned by
  * the caller and must stay alive until the stream has run the call.
  *
+ * Kernels are launched with programmatic dependent launch and release their
+ * successor at entry: a kernel of the caller's that follows one of ours on the
+ * same stream with programmatic stream serialisation must execute
+ * griddepcontrol.wait (cudaGridDependencySynchronize) before it reads our
+ * outputs.  Ordinary launches, copies and events order as usual.
+ *
  * Each entry point names the reference (moelan) interface it replaces.
  * Reference paths are relative to the moelan project root.
  */
