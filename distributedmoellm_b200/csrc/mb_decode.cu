@@ -377,7 +377,11 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
     const int64_t ctotal = cpre[E];
     const int64_t lo = item_at_cost(pre, cpre, cnt_s, E, RTS, ctotal * blockIdx.x / gridDim.x);
     const int64_t hi = item_at_cost(pre, cpre, cnt_s, E, RTS, ctotal * (blockIdx.x + 1) / gridDim.x);
-    if (lo >= hi) return;
+    if (lo >= hi) {
+        // nothing to do; still wait, so that this kernel completes only after the one before it
+        if (a.phase == 2) mb_pdl_wait();
+        return;
+    }
     const int64_t n_items = hi - lo;
     ItemCursor cur;
     cur.start(pre, E, RTS, lo);
