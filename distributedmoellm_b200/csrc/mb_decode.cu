@@ -31,6 +31,7 @@
 //  * Work items are (expert, chunk of 8 picks, MT row tiles), split
 //    contiguously over a persistent grid so each CTA touches one or two
 //    experts.
+#include <algorithm>
 #include <type_traits>
 
 #include "mb_common.cuh"
@@ -743,6 +744,18 @@ int dispatch_fmt(int fmt, F&& f)
     }
 }
 
+// Clears each pick's max |act| word before the gate|up phase, as one more kernel in the programmatic launch
+// chain (a memset node would break it): it is placed while the kernel before it drains, waits on it (the
+// last reader of these words, a previous call's down phase, is complete by then), clears, and lets the
+// gate|up phase launch.
+__global__ void clear_words_kernel(unsigned* __restrict__ words, int64_t n)
+{
+    mb_pdl_wait();
+    mb_pdl_trigger();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        words[i] = 0u;
+}
+
 __global__ void row_absmax_bits_kernel(const float* __restrict__ x, int64_t n, int K, unsigned* __restrict__ out)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -824,7 +837,8 @@ extern "C" int mb_moe_decode(const MbExpert* table, int E, int H, int I, int gs,
     unsigned* act_max = reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(workspace) +
                                                     ((P * I_pad * 4 + 255) / 256) * 256);
     unsigned* ws_status = reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(act_max) + ((P * 4 + 255) / 256) * 256);
-    cudaError_t e = cudaMemsetAsync(act_max, 0, P * sizeof(unsigned), st);
+    const unsigned nclr = (unsigned)std::min<int64_t>((P + 255) / 256, 148);
+    cudaError_t e = mb_launch_pdl(clear_words_kernel, dim3(nclr), dim3(256), 0, st, act_max, P);
     if (e != cudaSuccess) return mb_fail(MB_ECUDA, "mb_moe_decode: %s", cudaGetErrorString(e));
 
     DecodeArgs a{};
