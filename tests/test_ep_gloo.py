@@ -161,6 +161,17 @@ def test_ep_two_gloo_ranks_match_the_oracle():
         assert err < 1e-5, res
 
 
+def test_ep_four_gloo_ranks_match_the_oracle():
+    """Four ranks (two experts each here): uneven token counts per rank, every
+    rank's experts fed by all four."""
+    assert E % 4 == 0
+    res = _run(4)
+    for r in range(4):
+        kind, err = res[r]
+        assert kind == "ok", res
+        assert err < 1e-5, res
+
+
 def test_ep_rank_failure_surfaces_as_an_error():
     res = _run(2, fail_rank=1)
     assert res[1][0] == "raised", res
