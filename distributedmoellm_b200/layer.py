@@ -37,7 +37,8 @@ def run_experts(experts: LayerExperts, x: torch.Tensor, row_exp: torch.Tensor, r
                 workspace, status: torch.Tensor, gemm_min_rows: int, picks: int | None = None) -> None:
     """Every expert's picks through its gate|up, SiLU, down into y (one row
     per pick, in routing order): experts with at least gemm_min_rows picks as
-    grouped GEMMs on the tensor cores, the rest through the decode mat-vecs.
+    grouped GEMMs on the tensor cores, the rest through the decode mat-vecs
+    (every expert as a grouped GEMM once the picks average 2·gemm_min_rows).
     ``workspace(name, nbytes)`` returns a uint8 device buffer of at least
     nbytes that stays the same between calls of the same size.  ``picks``:
     the picks these experts get (default routing.P; smaller when routing
@@ -45,6 +46,11 @@ def run_experts(experts: LayerExperts, x: torch.Tensor, row_exp: torch.Tensor, r
     ex, P = experts, routing.P
     if gemm_only(ex):
         # the decode kernels take K <= 2048 and no affine format: every expert as a grouped GEMM
+        D.moe_prefill(ex.table, ex.eexp, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing, y,
+                      workspace("prefill", D.prefill_workspace_bytes(P, ex.H, ex.I, ex.fmt_gu)), min_rows=1, status=status)
+    elif uses_gemm(ex, P if picks is None else picks, gemm_min_rows) and (P if picks is None else picks) >= 2 * ex.E * gemm_min_rows:
+        # picks average at least twice gemm_min_rows per expert: few if any fall below it, and the decode
+        # launches for them would mostly find nothing to do; the grouped GEMM takes every expert
         D.moe_prefill(ex.table, ex.eexp, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing, y,
                       workspace("prefill", D.prefill_workspace_bytes(P, ex.H, ex.I, ex.fmt_gu)), min_rows=1, status=status)
     elif uses_gemm(ex, P if picks is None else picks, gemm_min_rows):
