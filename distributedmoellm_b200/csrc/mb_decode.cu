@@ -100,9 +100,12 @@ __device__ __forceinline__ int64_t items_of(int n, int max_rows, int RTS)
 // Estimated cost of the work, for splitting it over the CTAs: an item of a
 // chunk of at most 4 picks costs kCostOne, of 5..8 picks (both N tiles of the
 // MMAs live) kCostTwo, and the first item of a chunk kCostSwitch more (the
-// chunk's activation rows are gathered from global memory there).  Measured
-// on B200: 0.94 / 1.18 us per two-tile item, ~3 us per chunk switch.
-constexpr int kCostOne = 4, kCostTwo = 5, kCostSwitch = 12;
+// chunk's activation rows are gathered from global memory there).  Item
+// weights from per-item timings on B200 (0.94 / 1.18 us per two-tile item);
+// the switch weight is the best of 0, 3, 6, 12 and 20 in timed decode steps
+// (T = 32 and 64): with the rows kept in L2 a switch mostly overlaps the
+// stages already in flight.
+constexpr int kCostOne = 4, kCostTwo = 5, kCostSwitch = 3;
 
 __device__ __forceinline__ int64_t cost_of(int n, int max_rows, int RTS)
 {
