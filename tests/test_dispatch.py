@@ -1,0 +1,57 @@
+"""The layer's choice of kernels (layer.run_experts), on CPU with the device
+entry points replaced by recorders: the decode mat-vecs for small batches,
+both kernels for mid-sized ones (experts below gemm_min_rows picks on the
+decode kernel), every expert on the grouped GEMM once the picks average twice
+gemm_min_rows, and always the grouped GEMM for experts the decode kernel
+cannot take (affine int4, K > 2048)."""
+
+import sys
+import types
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+
+from distributedmoellm_b200 import layer as Lyr  # noqa: E402
+from distributedmoellm_b200 import layout as L  # noqa: E402
+
+
+def _experts(E=128, H=2048, I=768, fmt=L.FMT_Q4_F16):
+    return types.SimpleNamespace(E=E, H=H, I=I, gs=32, fmt_gu=fmt, fmt_down=fmt, table=None, eexp=None,
+                                 missing_exp=False)
+
+
+def _run(monkeypatch, ex, P, picks=None, m=32):
+    calls = []
+    monkeypatch.setattr(Lyr.D, "moe_decode", lambda *a, **k: calls.append(("decode", k.get("max_rows"))))
+    monkeypatch.setattr(Lyr.D, "moe_prefill", lambda *a, **k: calls.append(("gemm", k.get("min_rows"))))
+    monkeypatch.setattr(Lyr.D, "decode_workspace_bytes", lambda *a: 0)
+    monkeypatch.setattr(Lyr.D, "prefill_workspace_bytes", lambda *a: 0)
+    routing = types.SimpleNamespace(P=P)
+    Lyr.run_experts(ex, None, None, routing, None, lambda name, n: None, None, m, picks=picks)
+    return calls
+
+
+@pytest.mark.parametrize("T,want", [
+    (64, [("decode", 0)]),                               # decode batch: 512 picks over 128 experts
+    (256, [("decode", 31), ("gemm", 32)]),               # 2048 picks: 16 per expert on average
+    (1024, [("gemm", 1)]),                               # 8192 picks: 64 per expert, all on the GEMM
+    (2048, [("gemm", 1)]),
+])
+def test_kernel_choice_by_batch(monkeypatch, T, want):
+    assert _run(monkeypatch, _experts(), T * 8) == want
+
+
+def test_affine_and_wide_experts_always_use_the_gemm(monkeypatch):
+    assert _run(monkeypatch, _experts(fmt=L.FMT_Q4K_F32), 1) == [("gemm", 1)]
+    assert _run(monkeypatch, _experts(E=8, H=4096, I=14336, fmt=L.FMT_Q8_F16), 2) == [("gemm", 1)]
+
+
+def test_expert_parallel_slice_decides_by_its_own_picks(monkeypatch):
+    # a rank's 16 experts out of 128 see all ranks' picks in the routing; the choice follows its share
+    ex = _experts(E=16)
+    assert _run(monkeypatch, ex, 4096, picks=512) == [("decode", 31), ("gemm", 32)]
+    assert _run(monkeypatch, ex, 4096, picks=255) == [("decode", 0)]   # below 16 per expert on average
+    assert _run(monkeypatch, ex, 16384, picks=2048) == [("gemm", 1)]
