@@ -29,9 +29,9 @@ import threading
 import time
 from pathlib import Path
 
-if "--impl" in sys.argv and "reference" in sys.argv:
-    # the reference runs BLAS single-threaded and parallelises over experts
-    os.environ.setdefault("OPENBLAS_NUM_THREADS", "1")
+# the reference runs BLAS single-threaded and parallelises over experts
+# (moelan/__init__.py:9-12); both CPU timings below follow it
+os.environ["OPENBLAS_NUM_THREADS"] = "1"
 
 import numpy as np
 
@@ -45,6 +45,12 @@ L2_ROTATE_LAYERS = 4
 # T=64, from one ncu capture of `bench.py --profile` (the dominant kernel's
 # traffic; other token counts report None)
 NCU_DECODE_TRAFFIC = {64: 343_900_000}
+# this library's kernels per decode step: router logits + top-k, permute, the
+# decode's clear of its activation maxima, gate|up and down phases, combine
+LAUNCHES_PER_STEP = 7
+# expert parallelism adds no kernel of ours (NCCL all-gather and reduce-scatter,
+# one torch.where for the local pick mask)
+LAUNCHES_PER_EP_STEP = 7
 
 
 def parse():
@@ -61,6 +67,8 @@ def parse():
     p.add_argument("--profile-prefill", action="store_true",
                    help="only a few prefill steps of the int4 layer at 2048 tokens (for ncu)")
     p.add_argument("--no-prefill", action="store_true")
+    p.add_argument("--no-dropin", action="store_true", help="skip the drop-in moe_q4 end-to-end figure")
+    p.add_argument("--no-parity", action="store_true", help="skip the multi-GPU step's check against one GPU")
     return p.parse_args()
 
 
@@ -76,6 +84,7 @@ def make_experts(seed=0):
     rng = np.random.default_rng(seed)
     experts = {e: S.int4_expert(rng, H, I, GS, f16_scales=True) for e in range(E)}
     router = S.router(rng, E, H)
+    make_experts.router = router
     return experts, router
 
 
@@ -146,9 +155,9 @@ def measure_prefill(layer, T, steps, warmup, world, dev, seed=5):
 
     ms, ex_ms = timed(full, steps), timed(ex, steps)
     st = int(layer.status(T))
-    gemm = layer.uses_gemm(T)
+    plan = layer.kernel_plan(T)
     del full, ex
-    return ms, ex_ms, st, gemm
+    return ms, ex_ms, st, plan
 
 
 # ---- clocks sampled during the timed region ------------------------------------------
@@ -213,13 +222,28 @@ def cpu_step_fn(experts, router, T, seed=7):
     return step, O
 
 
-def time_cpu(step, budget_s=12.0, max_steps=200):
-    step()  # warm (thread pools, page-in)
+def host_threads() -> int:
+    """Host cores this process may run on (torchrun sets OMP_NUM_THREADS=1;
+    the CPU timings use every core regardless)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def time_cpu(step, O, warmup=1, max_steps=200, budget_s=12.0):
+    """The one CPU timing of the reference's algorithm, used by both the GPU
+    arm's cpu_baseline and the reference arm: the oracle's OpenMP threads set
+    to every host core, ``warmup`` untimed steps, then up to ``max_steps``
+    steps or ``budget_s`` seconds.  Returns (seconds per step, steps, threads)."""
+    O.set_threads(host_threads())
+    for _ in range(max(1, warmup)):
+        step()  # warm (thread pools, page-in)
     n, t0 = 0, time.perf_counter()
     while n < max_steps and (n == 0 or time.perf_counter() - t0 < budget_s):
         step()
         n += 1
-    return (time.perf_counter() - t0) / n, n
+    return (time.perf_counter() - t0) / n, n, O.threads()
 
 
 # ---- GPU side ---------------------------------------------------------------------------------
@@ -318,6 +342,19 @@ def run_gpu_ep(args, rank, world, dev):
         return max_over_ranks(a.elapsed_time(b) / steps)
 
     T = args.tokens
+    parity = {}
+    if not args.no_parity:
+        # the EP step's own output against one GPU holding every expert over all ranks' tokens
+        from distributedmoellm_b200.layer import MoELayer, kernel_plan
+        full = LayerExperts(E, H, I, GS, L.FMT_Q4_F16, L.FMT_Q4_F16, dev) if rank == 0 else None
+        if rank == 0:
+            for e in range(E):
+                full.put_int4(e, *experts[e])
+            full.publish()
+        ep_gemm = any(k == "gemm" for k, _ in kernel_plan(base, T * K_TOP, layers[0].gemm_min_rows))
+        parity["decode"] = ep_parity(layers[0], lambda: MoELayer(rt, full, K_TOP, True, gemm_min_rows=0),
+                                     T, rank, world, dev, 2e-3 if ep_gemm else 1e-5, 4000)
+        del full
     gpu_index = dev.index or 0
     with Clocks(gpu_index) as clk:
         ms = measure(layers, T, args.steps, args.warmup, 1000, graphs=True)
@@ -342,11 +379,53 @@ def run_gpu_ep(args, rank, world, dev):
                 q8.put_int8(e - rank * El, *parts)
         q8.publish()
         pl = [EPLayer(DeviceOps(rt, q8, E, K_TOP), E, K_TOP, H)]
+        if not args.no_parity:
+            def full_q8():
+                from distributedmoellm_b200.layer import MoELayer
+                rng8 = np.random.default_rng(3)
+                f8 = LayerExperts(E, H, I, GS, L.FMT_Q8_F32, L.FMT_Q8_F32, dev)
+                for e in range(E):
+                    f8.put_int8(e, *S.int8_expert(rng8, H, I, GS))
+                f8.publish()
+                return MoELayer(rt, f8, K_TOP, True)
+            parity["prefill_int8_T2048"] = ep_parity(pl[0], full_q8, 2048, rank, world, dev, 2e-3, 6000)
         for Tp in (2048,):
             m = measure(pl, Tp, max(10, args.steps // 8), 3, 3000)
             prefill[f"int8_T{Tp}_ep{world}"] = {"tokens_per_s": round(world * Tp / (m / 1e3), 1),
                                                "ms_per_step": round(m, 5)}
-    return value, ms, roof, e2e, {}, None, clk.summary(), 0, prefill
+    if parity:
+        prefill["parity"] = parity
+    return value, ms, roof, e2e, {}, None, clk.summary(), 0, prefill, None
+
+
+def ep_parity(ep_layer, make_full, T, rank, world, dev, bar, seed):
+    """One step of ``ep_layer`` on every rank's own T tokens, gathered to rank
+    0 and compared there with ``make_full()`` (one GPU holding every expert)
+    over all ranks' tokens in rank order, in chunks of at most 4096 tokens
+    (each token's result does not depend on the others in its batch).  The
+    error is max|ep - one| / max|one| per output row; returns
+    {"max_row_err", "bar", "ok", "tokens"} on rank 0, None elsewhere."""
+    import torch
+    import torch.distributed as dist
+    x = torch.from_numpy(np.random.default_rng(seed + rank).standard_normal((T, H), dtype=np.float32)).to(dev)
+    out = ep_layer(x).clone()
+    xs = [torch.empty_like(x) for _ in range(world)]
+    outs = [torch.empty_like(out) for _ in range(world)]
+    dist.all_gather(xs, x)
+    dist.all_gather(outs, out)
+    res = None
+    if rank == 0:
+        one = make_full()
+        xa = torch.cat(xs)
+        ref = torch.cat([one(xa[i:i + 4096]).clone() for i in range(0, xa.shape[0], 4096)])
+        got = torch.cat(outs).double()
+        ref = ref.double()
+        err = ((got - ref).abs().amax(dim=1) / ref.abs().amax(dim=1).clamp_min(1e-30)).max().item()
+        res = {"max_row_err": float(err), "bar": bar, "ok": bool(err <= bar and torch.isfinite(got).all().item()),
+               "tokens": int(xa.shape[0])}
+        del one
+    dist.barrier()
+    return res
 
 
 def run_gpu(args, rank, world, dev):
@@ -404,11 +483,11 @@ def run_gpu(args, rank, world, dev):
         if os.environ.get("CUDA_VISIBLE_DEVICES", "").replace(",", "").isdigit() else (dev.index or 0)
     if args.profile_prefill:
         ms, ex_ms, status, _ = measure_prefill(layers[0], 2048, args.steps, args.warmup, world, dev)
-        return world * 2048 / (ms / 1e3), ms, {}, {}, {}, None, {}, status, {}
+        return world * 2048 / (ms / 1e3), ms, {}, {}, {}, None, {}, status, {}, None
     with Clocks(gpu_index) as clk:
         ms, dec_ms, u_avg, status = measure(T, args.steps, args.warmup)
     if args.profile:
-        return world * T / (ms / 1e3), ms, {}, {}, {}, None, clk.summary(), status, {}
+        return world * T / (ms / 1e3), ms, {}, {}, {}, None, clk.summary(), status, {}, None
     ms = max_over_ranks(ms)
     value = world * T / (ms / 1e3)
 
@@ -442,11 +521,12 @@ def run_gpu(args, rank, world, dev):
         l8 = int8_layer(router, dev)
         tf_peak = pk.get("bf16_tflops", 1590.0)
         for name, layer, Tp in (("int8_T2048", l8, 2048), ("int8_T4096", l8, 4096), ("int4_T2048", layers[0], 2048)):
-            m, em, st, gemm = measure_prefill(layer, Tp, max(10, args.steps // 8), 3, world, dev)
+            m, em, st, plan = measure_prefill(layer, Tp, max(10, args.steps // 8), 3, world, dev)
             m, em = max_over_ranks(m), max_over_ranks(em)
             fl = Tp * PREFILL_FLOPS_PER_TOKEN
             prefill[name] = {"tokens_per_s": round(world * Tp / (m / 1e3), 1), "ms_per_step": round(m, 5),
-                             "experts_ms": round(em, 5), "grouped_gemm": gemm,
+                             "experts_ms": round(em, 5), "grouped_gemm": any(k == "gemm" for k, _ in plan),
+                             "kernels": [list(p) for p in plan],
                              "roofline": {"bound": "tensor", "achieved": round(fl / (em / 1e3) / 1e12, 1),
                                           "peak": tf_peak, "unit": "TFLOP/s",
                                           "frac": round(fl / (em / 1e3) / 1e12 / tf_peak, 4),
@@ -458,12 +538,13 @@ def run_gpu(args, rank, world, dev):
         lg = gguf_layer(dev)
         bytes_per_expert = 2 * (14336 * 4096 // 256 * 144) + 4096 * (14336 // 32 * 34)
         for Tp in (1, 512):
-            m, em, st, gemm = measure_prefill(lg, Tp, max(10, args.steps // 8), 3, world, dev)
+            m, em, st, plan = measure_prefill(lg, Tp, max(10, args.steps // 8), 3, world, dev)
             m, em = max_over_ranks(m), max_over_ranks(em)
             fl = Tp * 2 * 2 * 3 * 4096 * 14336
             used = min(8, 2 * Tp)
             ent = {"tokens_per_s": round(world * Tp / (m / 1e3), 1), "ms_per_step": round(m, 5),
-                   "experts_ms": round(em, 5), "grouped_gemm": True,
+                   "experts_ms": round(em, 5), "grouped_gemm": any(k == "gemm" for k, _ in plan),
+                   "kernels": [list(p) for p in plan],
                    "tflops": round(fl / (em / 1e3) / 1e12, 1),
                    "hbm_gbs": round(used * bytes_per_expert / (em / 1e3) / 1e9, 1)}
             ent["roofline"] = ({"bound": "hbm", "achieved": ent["hbm_gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
@@ -474,14 +555,66 @@ def run_gpu(args, rank, world, dev):
             status = max(status, st)
         del lg
 
+    # end to end through the reference-facing drop-in: moelan's own call moe_q4(x, items, H, I, gs, out)
+    # with pageable numpy arrays (moelan/experts.py:729-753)
+    e2e_dropin = None
+    if not args.no_dropin:
+        dm = measure_dropin(experts, T, max(10, args.steps // 20), 3)
+        e2e_dropin = {"value": round(world * T / (dm / 1e3), 1), "unit": UNIT, "ms_per_step": round(dm, 4),
+                      "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": None,
+                      "api": "distributedmoellm_b200.kernels.moe_q4 (the install() replacement of "
+                             "moelan.kernels.moe_q4), numpy in and out; moelan's host routing before the call "
+                             "is not timed"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         step, O = cpu_step_fn(experts, router, T)
-        s_per, n = time_cpu(step)
-        cpu = {"value": round(T / s_per, 2), "unit": UNIT, "cores": O.threads(), "kind": "port",
+        s_per, n, thr = time_cpu(step, O)
+        cpu = {"value": round(T / s_per, 2), "unit": UNIT, "cores": thr, "kind": "port",
                "sample": f"{n} MoE-layer steps of T={T} tokens (all 128 experts resident in host RAM), "
                          f"C+OpenMP restatement of moelan's fused int4 layer kernel + numpy routing"}
-    return value, ms, roof, e2e, sweep, cpu, clk.summary(), status, prefill
+    return value, ms, roof, e2e, sweep, cpu, clk.summary(), status, prefill, e2e_dropin
+
+
+def measure_dropin(experts, T, steps, warmup):
+    """ms per call of the drop-in moe_q4 with moelan's own arguments: items of
+    (q4_expert_ptrs(expert), rows, weights) over host arrays (f32 scales, as
+    moelan's fused path requires, kernels.py:929-939), x and out pageable
+    numpy; the call copies x in, runs the kernels and adds the result into out
+    on the host.  Four token sets with their own routings rotate."""
+    import types
+    from distributedmoellm_b200 import kernels as Kn
+    NS = types.SimpleNamespace
+    objs = {}
+    for e, (gr, gsc, dr, dsc) in experts.items():
+        gu = NS(raw=gr, s=np.ascontiguousarray(gsc, np.float32), gs=GS, offset=False)
+        dn = NS(raw=dr, s=np.ascontiguousarray(dsc, np.float32), gs=GS, offset=False)
+        objs[e] = NS(gu=gu, down=dn)
+    router = make_experts.router
+    sets = []
+    for i in range(4):
+        x = np.random.default_rng(5000 + i).standard_normal((T, H), dtype=np.float32)
+        logits = x @ router.T                                       # moelan/model.py:597, 154-167, 226-236
+        z = np.exp(logits - logits.max(-1, keepdims=True))
+        probs = z / z.sum(-1, keepdims=True)
+        idx = np.argsort(-probs, axis=-1, kind="stable")[:, :K_TOP]
+        w = np.take_along_axis(probs, idx, axis=-1)
+        w = (w / w.sum(-1, keepdims=True)).astype(np.float32)
+        order = np.argsort(idx.reshape(-1), kind="stable")
+        es, starts = np.unique(idx.reshape(-1)[order], return_index=True)
+        offs = np.append(starts, T * K_TOP)
+        items = [(Kn.q4_expert_ptrs(objs[int(e)]), order[offs[j]:offs[j + 1]] // K_TOP,
+                  w.reshape(-1)[order[offs[j]:offs[j + 1]]]) for j, e in enumerate(es)]
+        sets.append((x, items))
+    out = np.zeros((T, H), np.float32)
+    for i in range(warmup):
+        x, items = sets[i % 4]
+        Kn.moe_q4(x, items, H, I, GS, out)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        x, items = sets[i % 4]
+        Kn.moe_q4(x, items, H, I, GS, out)
+    return (time.perf_counter() - t0) / steps * 1e3
 
 
 def measure_e2e(layers, T, steps, warmup, world, dev):
@@ -522,24 +655,18 @@ def measure_e2e(layers, T, steps, warmup, world, dev):
 
 
 def run_reference(args):
-    """The reference arm: moelan's CPU algorithm (oracle restatement) on the host cores."""
+    """The reference arm: moelan's CPU algorithm (oracle restatement) on all host cores."""
     experts, router = make_experts(0)
     step, O = cpu_step_fn(experts, router, args.tokens)
-    for _ in range(max(1, args.warmup)):
-        step()
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        step()
-        times.append(time.perf_counter() - t0)
-    ms = 1e3 * statistics.mean(times)
+    s_per, n, thr = time_cpu(step, O, warmup=args.warmup, max_steps=args.steps, budget_s=120.0)
+    ms = 1e3 * s_per
     value = args.tokens / (ms / 1e3)
     return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "impl": "reference",
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": workload_config(args),
-            "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": O.threads(), "kind": "port",
-                             "sample": f"{args.steps} MoE-layer steps of T={args.tokens}"},
+            "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": thr, "kind": "port",
+                             "sample": f"{n} MoE-layer steps of T={args.tokens}"},
             "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -570,9 +697,9 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     if world > 1:
-        value, ms, roof, e2e, sweep, cpu, clocks, status, prefill = run_gpu_ep(args, rank, world, dev)
+        value, ms, roof, e2e, sweep, cpu, clocks, status, prefill, dropin = run_gpu_ep(args, rank, world, dev)
     else:
-        value, ms, roof, e2e, sweep, cpu, clocks, status, prefill = run_gpu(args, rank, world, dev)
+        value, ms, roof, e2e, sweep, cpu, clocks, status, prefill, dropin = run_gpu(args, rank, world, dev)
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
@@ -580,8 +707,9 @@ def main():
                 "dtype_note": "decode: int4 weights x f32 activations, products exact (f16 pieces), f32 sums; "
                               "prefill: f16 tensor-core operands with power-of-two range scaling, f32 sums",
                 "data": "synthetic", "config": workload_config(args), "roofline": roof, "cpu_baseline": cpu,
-                "e2e": e2e, "clocks": clocks, "gpu_launches": (6 if world == 1 else 9) * args.steps, "sweep": sweep,
-                "prefill": prefill, "kernel_status": status}
+                "e2e": e2e, "e2e_dropin": dropin, "clocks": clocks,
+                "gpu_launches": (LAUNCHES_PER_STEP if world == 1 else LAUNCHES_PER_EP_STEP) * args.steps,
+                "sweep": sweep, "prefill": prefill, "kernel_status": status}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -22,6 +22,7 @@ SIGNATURES = {
     "mb_q4_dequant": (_int, [_vp, _vp, _int, _i64, _i64, _int, _u8, _vp, _vp]),
     "mb_q8_dequant": (_int, [_vp, _vp, _int, _i64, _i64, _int, _vp, _vp]),
     "mb_gguf_dequant": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _vp]),
+    "mb_gguf_matmul_t": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),
     "mb_router_workspace_bytes": (_i64, [_i64, _int, _int]),
     "mb_router_logits": (_int, [_vp, _vp, _i64, _int, _int, _vp, _vp, _vp, _i64, _vp]),
     "mb_router_route": (_int, [_vp, _vp, _i64, _int, _int, _int, _int, _vp, _vp, _vp, _vp, _vp, _i64, _vp]),

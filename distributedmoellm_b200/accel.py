@@ -42,6 +42,7 @@ class DevicePool:
         self.device = torch.device(device)
         self.entries: dict = {}          # key -> (Packed, buffer, gu address, down address)
         self._ws: dict = {}
+        self._ws_lock = threading.Lock()
 
     def put(self, key, packed) -> int:
         g = torch.from_numpy(np.ascontiguousarray(packed.gu_tiles))
@@ -58,10 +59,14 @@ class DevicePool:
         return buf.numel()
 
     def workspace(self, name, nbytes):
-        b = self._ws.get(name)
-        if b is None or b.numel() < nbytes:
-            b = self._ws[name] = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=self.device)
-        return b
+        """A device buffer of at least nbytes, reused by later calls on this
+        pool's stream order (the kernels of one call finish before the next
+        call's reuse them: all run on the caller's current stream)."""
+        with self._ws_lock:
+            b = self._ws.get(name)
+            if b is None or b.numel() < nbytes:
+                b = self._ws[name] = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=self.device)
+            return b
 
     def compute(self, x: torch.Tensor, keys, rows, weights, gemm_min_rows: int = 32):
         """Weighted expert outputs summed per input row: returns (unique rows,
@@ -75,8 +80,7 @@ class DevicePool:
         P = len(all_rows)
         y = torch.empty((max(P, 1), H), dtype=torch.float32, device=self.device)
         row_exp = D.row_exponents(x)
-        status = self.workspace("status", 4).view(torch.int32)[:1]
-        status.zero_()
+        status = torch.zeros(1, dtype=torch.int32, device=self.device)     # this call's own status word
         # experts of one signature share a launch
         sigs: dict = {}
         for i, k in enumerate(keys):

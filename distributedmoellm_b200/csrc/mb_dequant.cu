@@ -6,6 +6,8 @@
 //   int4  moelan/kernels.py:215-228   f32(nibble - 8) * s
 //   int8  moelan/kernels.py:230-237   f32(q) * s
 //   GGUF  moelan/kernels.py:262-476   llama.cpp block formats
+#include <algorithm>
+
 #include "mb_common.cuh"
 
 namespace {
@@ -66,7 +68,7 @@ __device__ __forceinline__ void scale_min_k4(int j, const uint8_t* s, int& sc, i
     }
 }
 
-__device__ void gguf_segment(const uint8_t* row, int qtype, int64_t seg, float* v)
+__device__ __forceinline__ void gguf_segment(const uint8_t* row, int qtype, int64_t seg, float* v)
 {
     switch (qtype) {
     case 8: {  // Q8_0, kernels.py:262-268
@@ -214,6 +216,53 @@ __global__ void gguf_dequant_kernel(const uint8_t* __restrict__ raw, int qtype, 
     }
 }
 
+// x @ W.T straight from GGUF blocks for a few input rows (decode): one warp per
+// weight row, each lane decoding 32-value segments with the bit-exact block
+// decoders above and dotting them with up to NR input rows in f32.  QT: the
+// ggml type id (a compile-time constant, so each decoder is specialised).
+template <int QT, int NR>
+__global__ void __launch_bounds__(256) gguf_mv_kernel(const uint8_t* __restrict__ raw, int64_t rows,
+                                                      int64_t row_bytes, int64_t cols, const float* __restrict__ x,
+                                                      int n, float* __restrict__ y)
+{
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t nseg = cols / 32;
+    for (int64_t o = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); o < rows; o += warps) {
+        const uint8_t* row = raw + o * row_bytes;
+        float acc[NR];
+#pragma unroll
+        for (int r = 0; r < NR; ++r) acc[r] = 0.0f;
+        for (int64_t seg = lane; seg < nseg; seg += 32) {
+            float v[32];
+            gguf_segment(row, QT, seg, v);
+#pragma unroll
+            for (int r = 0; r < NR; ++r) {
+                if (r < n) {
+                    const float4* xp = reinterpret_cast<const float4*>(x + (int64_t)r * cols + seg * 32);
+                    float s = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float4 u = __ldg(xp + j);
+                        s = fmaf(v[4 * j], u.x, s);
+                        s = fmaf(v[4 * j + 1], u.y, s);
+                        s = fmaf(v[4 * j + 2], u.z, s);
+                        s = fmaf(v[4 * j + 3], u.w, s);
+                    }
+                    acc[r] += s;
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+            float a = acc[r];
+#pragma unroll
+            for (int off = 16; off; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+            if (lane == 0 && r < n) y[(int64_t)r * rows + o] = a;
+        }
+    }
+}
+
 int grid_for(int64_t n, int block)
 {
     int64_t g = (n + block - 1) / block;
@@ -286,4 +335,52 @@ extern "C" int mb_gguf_dequant(const uint8_t* raw, int qtype, int64_t rows, int6
     if (n == 0) return MB_OK;
     gguf_dequant_kernel<<<grid_for(n, 128), 128, 0, mb_stream(stream)>>>(raw, qtype, rows, row_bytes, cols, out);
     return mb_check_launch("mb_gguf_dequant");
+}
+
+// x @ W.T for a GGUF block-quantised W (rows, row_bytes), a few input rows at a
+// time: moelan/kernels.py:981-998 gguf_matmul_t (fused per-type mat-vecs
+// _mv_q8_0 482-497, _mv_q4_k 499-527, _mv_q5_k, _mv_q2_k, _mv_q3_k, _mv_q6_k
+// 529-676, and the row-decoding _gguf_mm for the other types), every type of
+// mb_gguf_dequant.  x (n, cols) f32, y (n, rows) f32, both 16-byte aligned.
+extern "C" int mb_gguf_matmul_t(const uint8_t* raw, int qtype, int64_t rows, int64_t row_bytes, int64_t cols,
+                                const float* x, int64_t n, float* y, void* stream)
+{
+    int vals = 0, bytes = 0;
+    MB_REQUIRE(raw && x && y, "mb_gguf_matmul_t: null pointer");
+    if (!gguf_block(qtype, &vals, &bytes)) return mb_fail(MB_EUNSUPPORTED, "mb_gguf_matmul_t: GGUF type %d", qtype);
+    MB_REQUIRE(rows >= 0 && n >= 0 && cols > 0 && cols % vals == 0 && row_bytes == cols / vals * bytes,
+               "mb_gguf_matmul_t: cols=%lld row_bytes=%lld do not fit type %d", (long long)cols,
+               (long long)row_bytes, qtype);
+    MB_REQUIRE(((uintptr_t)x & 15) == 0, "mb_gguf_matmul_t: x must be 16-byte aligned");
+    if (rows == 0 || n == 0) return MB_OK;
+    cudaStream_t st = mb_stream(stream);
+    const int grid = grid_for(rows * 32, 256);
+    for (int64_t r0 = 0; r0 < n; r0 += 8) {
+        const int nr = (int)std::min<int64_t>(8, n - r0);
+        const float* xr = x + r0 * cols;
+        float* yr = y + r0 * rows;
+#define MB_GGUF_MV(QT)                                                                                      \
+    case QT:                                                                                                \
+        if (nr == 1) gguf_mv_kernel<QT, 1><<<grid, 256, 0, st>>>(raw, rows, row_bytes, cols, xr, nr, yr);   \
+        else if (nr <= 4) gguf_mv_kernel<QT, 4><<<grid, 256, 0, st>>>(raw, rows, row_bytes, cols, xr, nr, yr); \
+        else gguf_mv_kernel<QT, 8><<<grid, 256, 0, st>>>(raw, rows, row_bytes, cols, xr, nr, yr);            \
+        break;
+        switch (qtype) {
+            MB_GGUF_MV(2)
+            MB_GGUF_MV(3)
+            MB_GGUF_MV(6)
+            MB_GGUF_MV(7)
+            MB_GGUF_MV(8)
+            MB_GGUF_MV(10)
+            MB_GGUF_MV(11)
+            MB_GGUF_MV(12)
+            MB_GGUF_MV(13)
+            MB_GGUF_MV(14)
+        default: break;
+        }
+#undef MB_GGUF_MV
+        const int rc = mb_check_launch("mb_gguf_matmul_t");
+        if (rc) return rc;
+    }
+    return MB_OK;
 }

@@ -38,6 +38,7 @@
 // the order in which the packed nibbles / bytes unpack into f16 pairs.
 #include <cuda.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "mb_common.cuh"
@@ -667,9 +668,9 @@ __global__ void gather_f16_kernel(const float* __restrict__ x, const int32_t* __
                                   const int32_t* __restrict__ row_exp, int64_t P, int H, __half* __restrict__ xp,
                                   __half* __restrict__ xp_lo)
 {
-    const int64_t p = blockIdx.y;
     const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
-    if (p >= P || c >= H) return;
+    if (c >= H) return;
+    for (int64_t p = blockIdx.y; p < P; p += gridDim.y) {   // gridDim.y <= 65535
     const int64_t row = sorted_rows[p];
     const float sc = pow2i(clamp120(row_exp[row]));
     float4 lo = *reinterpret_cast<const float4*>(x + row * H + c);
@@ -685,6 +686,7 @@ __global__ void gather_f16_kernel(const float* __restrict__ x, const int32_t* __
         const float4 rl = make_float4(lo.x - a.x, lo.y - b.x, lo.z - c2.x, lo.w - d.x);
         const float4 rh = make_float4(hi.x - a.y, hi.y - b.y, hi.z - c2.y, hi.w - d.y);
         *reinterpret_cast<uint4*>(xp_lo + p * H + c) = pack8_perm(rl, rh, 1.0f);
+    }
     }
 }
 
@@ -833,7 +835,7 @@ extern "C" int mb_moe_prefill(const MbExpert* table, const int32_t* e_exp, int E
     MB_REQUIRE(gs % 32 == 0 && H % gs == 0 && I % gs == 0, "mb_moe_prefill: group size %d", gs);
     MB_REQUIRE(((uintptr_t)x & 15) == 0 && ((uintptr_t)workspace & 15) == 0,
                "mb_moe_prefill: x and workspace must be 16-byte aligned");
-    MB_REQUIRE(P <= 65535, "mb_moe_prefill: P=%lld above 65535", (long long)P);
+    MB_REQUIRE(P <= 65536, "mb_moe_prefill: P=%lld above 65536 (the limit of mb_permute)", (long long)P);
     MB_REQUIRE(workspace_bytes >= mb_moe_prefill_workspace_bytes(P, H, I, fmt_gu),
                "mb_moe_prefill: workspace too small");
     if (P == 0) return MB_OK;
@@ -853,7 +855,7 @@ extern "C" int mb_moe_prefill(const MbExpert* table, const int32_t* e_exp, int E
         cudaMemsetAsync(status, 0, sizeof(unsigned), st);
     }
 
-    gather_f16_kernel<<<dim3((H / 8 + 127) / 128, (unsigned)P), 128, 0, st>>>(x, sorted_rows, row_exp, P, H, xp,
+    gather_f16_kernel<<<dim3((H / 8 + 127) / 128, (unsigned)std::min<int64_t>(P, 65535)), 128, 0, st>>>(x, sorted_rows, row_exp, P, H, xp,
                                                                             xp_lo);
     int rc = mb_check_launch("mb_moe_prefill gather");
     if (rc) return rc;

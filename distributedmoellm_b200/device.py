@@ -68,6 +68,16 @@ def gguf_dequant(raw: torch.Tensor, qtype: int, cols: int, out: torch.Tensor | N
     return out
 
 
+def gguf_matmul_t(raw: torch.Tensor, qtype: int, cols: int, x: torch.Tensor, y: torch.Tensor | None = None):
+    """x @ W.T straight from the GGUF blocks of W (rows, row_bytes)."""
+    _cuda(raw, x, y)
+    n = x.shape[0]
+    y = torch.empty((n, raw.shape[0]), dtype=torch.float32, device=x.device) if y is None else y
+    check(lib().mb_gguf_matmul_t(_p(raw), int(qtype), raw.shape[0], raw.shape[1], cols, _p(x), n, _p(y),
+                                 _stream()), "mb_gguf_matmul_t")
+    return y
+
+
 # ---- router -------------------------------------------------------------------------
 
 def router_workspace_bytes(T: int, H: int, E: int) -> int:

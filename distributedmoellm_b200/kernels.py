@@ -11,11 +11,17 @@ Weight matrices are packed into the device tile layout on first use and kept
 (keyed by the arrays' addresses, shapes and dtypes, holding a reference so
 the address cannot be reused while cached): like the reference's resident
 experts (kernels.py:942-947), they must not change while they are in use.
+
+moelan calls these from several host threads at once (its worker's server
+threads, the batcher thread, its BLAS pool): the caches are guarded by one
+re-entrant lock, which is held across each call's device work and result
+copy, so concurrent calls are serialised rather than interleaved.
 """
 
 from __future__ import annotations
 
 import ctypes
+import threading
 from collections import OrderedDict
 
 import numpy as np
@@ -27,9 +33,12 @@ from .accel import DevicePool
 from .packing import Packed
 
 _CACHE_MAX = 512
-_mats: OrderedDict = OrderedDict()        # matrix key -> (device tiles, fmt, O, K, kept arrays)
-_pool: dict = {}                          # device index -> DevicePool of moe_q4 experts
-_pool_keys: OrderedDict = OrderedDict()
+_lock = threading.RLock()                 # guards the caches below and each call's use of them
+_mats: OrderedDict = OrderedDict()        # matrix key -> (device tiles or raw blocks, fmt, O, K, kept arrays)
+_pool: dict = {}                          # device index -> (DevicePool of moe_q4 experts, their keys in use order)
+# the decode mat-vec kernel on the tile layout takes K up to this; wider GGUF
+# matrices go through the raw-block kernel
+_TILE_MAX_K = 2048
 
 
 def _dev():
@@ -42,6 +51,8 @@ def _key(*arrays):
 
 
 def _tiles(key, make, keep):
+    """The cached device copy for ``key`` (made by ``make()`` on a miss); call with _lock held."""
+    key = key + (_dev().index,)
     hit = _mats.get(key)
     if hit is not None:
         _mats.move_to_end(key)
@@ -54,10 +65,11 @@ def _tiles(key, make, keep):
     return ent
 
 
-def _matmul(ent, x):
-    t, fmt, O, K, _ = ent
-    xd = torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(t.device)
-    return D.matmul_t(t, fmt, O, K, xd).cpu().numpy()
+def _matmul(key, make, keep, x):
+    with _lock:
+        t, fmt, O, K, _ = _tiles(key, make, keep)
+        xd = torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(t.device)
+        return D.matmul_t(t, fmt, O, K, xd).cpu().numpy()
 
 
 # ---- dequantisation (moelan/kernels.py:971-1003) ------------------------------------
@@ -91,29 +103,38 @@ def q4_matmul_t(x: np.ndarray, raw: np.ndarray, s: np.ndarray, gs: int, offset: 
     def make():
         O, K = raw.shape[0], raw.shape[1] * 2
         return layout.fmt_of("q4", s), O, K, layout.q4_tiles(raw, s, gs, offset)
-    return _matmul(_tiles(_key(raw, s) + (gs, bool(offset)), make, (raw, s)), x)
+    return _matmul(_key(raw, s) + (gs, bool(offset)), make, (raw, s), x)
 
 
 def q8_matmul_t(x: np.ndarray, q: np.ndarray, s: np.ndarray, gs: int) -> np.ndarray:
     def make():
         return layout.fmt_of("q8", s), q.shape[0], q.shape[1], layout.q8_tiles(q, s, gs)
-    return _matmul(_tiles(_key(q, s) + (gs,), make, (q, s)), x)
+    return _matmul(_key(q, s) + (gs,), make, (q, s), x)
 
 
 def gguf_matmul_t(x: np.ndarray, raw: np.ndarray, qtype: int, cols: int) -> np.ndarray:
-    """x @ W.T for GGUF blocks: Q8_0 and Q4_0 (as int8 / int4 tiles with their
-    f16 block scales)."""
-    if qtype == 8:
-        def make():
-            q, d = layout.q8_0_as_q8(raw, cols)
-            return layout.FMT_Q8_F16, raw.shape[0], cols, layout.q8_tiles(q, d, 32)
-    elif qtype == 2:
-        def make():
-            r, d = layout.q4_0_as_q4(raw, cols)
-            return layout.FMT_Q4_F16, raw.shape[0], cols, layout.q4_tiles(r, d, 32, True)
-    else:
-        raise RuntimeError(f"gguf_matmul_t: GGUF type {qtype} has no device tile format in this build")
-    return _matmul(_tiles(_key(raw) + (int(qtype), cols), make, (raw,)), x)
+    """x @ W.T for GGUF blocks of any type moelan reads (moelan/kernels.py:981-998):
+    Q8_0 and Q4_0 up to K = 2048 as int8 / int4 tiles with their f16 block scales
+    (the tensor-core mat-vec), every other case straight from the blocks
+    (mb_gguf_matmul_t)."""
+    qtype = int(qtype)
+    if qtype in (8, 2) and cols <= _TILE_MAX_K:
+        if qtype == 8:
+            def make():
+                q, d = layout.q8_0_as_q8(raw, cols)
+                return layout.FMT_Q8_F16, raw.shape[0], cols, layout.q8_tiles(q, d, 32)
+        else:
+            def make():
+                r, d = layout.q4_0_as_q4(raw, cols)
+                return layout.FMT_Q4_F16, raw.shape[0], cols, layout.q4_tiles(r, d, 32, True)
+        return _matmul(_key(raw) + (qtype, cols), make, (raw,), x)
+
+    def make_raw():
+        return 0, raw.shape[0], cols, np.ascontiguousarray(raw, np.uint8)
+    with _lock:
+        t, _, _, _, _ = _tiles(_key(raw) + (qtype, cols, "raw"), make_raw, (raw,))
+        xd = torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(t.device)
+        return D.gguf_matmul_t(t, qtype, cols, xd).cpu().numpy()
 
 
 # ---- the fused int4 layer call (moelan/kernels.py:930-968) ------------------------------
@@ -143,10 +164,15 @@ def moe_q4(x: np.ndarray, items, H: int, I: int, gs: int, out: np.ndarray) -> No
     experts in one call.  ``items``: (ptrs from :func:`q4_expert_ptrs`, rows,
     gate weights) per expert; the arrays behind the pointers must stay alive
     and unchanged (each expert is uploaded on first use and kept)."""
+    with _lock:
+        _moe_q4(x, items, H, I, gs, out)
+
+
+def _moe_q4(x, items, H, I, gs, out):
     dev = _dev()
-    pool = _pool.get(dev.index)
-    if pool is None:
-        pool = _pool[dev.index] = DevicePool(dev)
+    if dev.index not in _pool:
+        _pool[dev.index] = (DevicePool(dev), OrderedDict())
+    pool, order = _pool[dev.index]
     keys = []
     for ptrs, _, _ in items:
         key = (tuple(int(p) for p in ptrs), H, I, gs)
@@ -161,10 +187,11 @@ def moe_q4(x: np.ndarray, items, H: int, I: int, gs: int, out: np.ndarray) -> No
             pool.put(key, Packed(layout.FMT_Q4_F32, layout.FMT_Q4_F32, gs, H, I,
                                  layout.q4_tiles(g_raw, g_s, gs, off, gu_inter=I), layout.q4_tiles(d_raw, d_s, gs, off),
                                  eexp))
-            _pool_keys[key] = None
-            while len(_pool_keys) > _CACHE_MAX:
-                pool.pop(_pool_keys.popitem(last=False)[0])
+        order[key] = None
+        order.move_to_end(key)
         keys.append(key)
+    while len(order) > max(_CACHE_MAX, len(keys)):      # never evict an expert this call uses
+        pool.pop(order.popitem(last=False)[0])
     xd = torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(dev)
     uniq, part, status = pool.compute(xd, keys, [r for _, r, _ in items], [w for _, _, w in items])
     out[uniq] += part.cpu().numpy()

@@ -23,7 +23,7 @@ def uses_gemm(experts: LayerExperts, P: int, gemm_min_rows: int) -> bool:
     (prefill-sized batches) and the shape allows them (H % 128, I % 64)."""
     m = gemm_min_rows
     return (m > 0 and experts.H % 128 == 0 and experts.I % 64 == 0 and 2 * P >= experts.E * m
-            and P <= 65535 and not experts.missing_exp)
+            and P <= 65536 and not experts.missing_exp)
 
 
 def gemm_only(experts) -> bool:
@@ -33,36 +33,45 @@ def gemm_only(experts) -> bool:
     return (FMT_Q4K_F32 in (experts.fmt_gu, experts.fmt_down) or experts.H > 2048 or experts.I > 2048)
 
 
+def kernel_plan(experts, P: int, gemm_min_rows: int) -> list:
+    """Which kernels run for P picks over these experts, in launch order:
+    ("decode", max_rows) and / or ("gemm", min_rows).  Experts the decode
+    kernels cannot take always run as grouped GEMMs; otherwise the GEMM runs
+    only for prefill-sized batches (see uses_gemm), over every expert once the
+    picks average twice gemm_min_rows (the decode launches would mostly find
+    nothing to do), else over the experts with at least gemm_min_rows picks
+    with the rest on the decode kernels."""
+    if gemm_only(experts):
+        return [("gemm", 1)]
+    if uses_gemm(experts, P, gemm_min_rows):
+        if P >= 2 * experts.E * gemm_min_rows:
+            return [("gemm", 1)]
+        return [("decode", gemm_min_rows - 1), ("gemm", gemm_min_rows)]
+    return [("decode", 0)]
+
+
 def run_experts(experts: LayerExperts, x: torch.Tensor, row_exp: torch.Tensor, routing, y: torch.Tensor,
                 workspace, status: torch.Tensor, gemm_min_rows: int, picks: int | None = None) -> None:
     """Every expert's picks through its gate|up, SiLU, down into y (one row
-    per pick, in routing order): experts with at least gemm_min_rows picks as
-    grouped GEMMs on the tensor cores, the rest through the decode mat-vecs
-    (every expert as a grouped GEMM once the picks average 2·gemm_min_rows).
+    per pick, in routing order), with the kernels of :func:`kernel_plan`.
     ``workspace(name, nbytes)`` returns a uint8 device buffer of at least
     nbytes that stays the same between calls of the same size.  ``picks``:
     the picks these experts get (default routing.P; smaller when routing
     covers other ranks' experts too), for the choice of kernels."""
     ex, P = experts, routing.P
-    if gemm_only(ex):
-        # the decode kernels take K <= 2048 and no affine format: every expert as a grouped GEMM
-        D.moe_prefill(ex.table, ex.eexp, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing, y,
-                      workspace("prefill", D.prefill_workspace_bytes(P, ex.H, ex.I, ex.fmt_gu)), min_rows=1, status=status)
-    elif uses_gemm(ex, P if picks is None else picks, gemm_min_rows) and (P if picks is None else picks) >= 2 * ex.E * gemm_min_rows:
-        # picks average at least twice gemm_min_rows per expert: few if any fall below it, and the decode
-        # launches for them would mostly find nothing to do; the grouped GEMM takes every expert
-        D.moe_prefill(ex.table, ex.eexp, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing, y,
-                      workspace("prefill", D.prefill_workspace_bytes(P, ex.H, ex.I, ex.fmt_gu)), min_rows=1, status=status)
-    elif uses_gemm(ex, P if picks is None else picks, gemm_min_rows):
-        D.moe_decode(ex.table, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing, y,
-                     workspace("decode", D.decode_workspace_bytes(P, ex.I)), max_rows=gemm_min_rows - 1,
-                     status=status)
-        D.moe_prefill(ex.table, ex.eexp, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing, y,
-                      workspace("prefill", D.prefill_workspace_bytes(P, ex.H, ex.I, ex.fmt_gu)), min_rows=gemm_min_rows,
-                      status=status)
-    else:
-        D.moe_decode(ex.table, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing, y,
-                     workspace("decode", D.decode_workspace_bytes(P, ex.I)), max_rows=0, status=status)
+    plan = kernel_plan(ex, P if picks is None else picks, gemm_min_rows)
+    if gemm_only(ex) and ex.missing_exp:
+        raise ValueError(f"experts {sorted(ex.missing_exp)[:8]} were stored without the exponents the "
+                         f"grouped GEMM needs (put_tiles(..., eexp=None)), and this layer's format or size "
+                         f"(fmt_gu={ex.fmt_gu}, H={ex.H}, I={ex.I}) runs only as grouped GEMMs")
+    for kind, rows in plan:
+        if kind == "decode":
+            D.moe_decode(ex.table, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing, y,
+                         workspace("decode", D.decode_workspace_bytes(P, ex.I)), max_rows=rows, status=status)
+        else:
+            D.moe_prefill(ex.table, ex.eexp, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing,
+                          y, workspace("prefill", D.prefill_workspace_bytes(P, ex.H, ex.I, ex.fmt_gu)),
+                          min_rows=rows, status=status)
 
 
 class _Buffers:
@@ -102,7 +111,12 @@ class MoELayer:
         self._bufs: dict[int, _Buffers] = {}
 
     def uses_gemm(self, T: int) -> bool:
-        return uses_gemm(self.experts, T * self.k, self.gemm_min_rows)
+        """Whether the grouped-GEMM kernels run for T tokens."""
+        return any(kind == "gemm" for kind, _ in self.kernel_plan(T))
+
+    def kernel_plan(self, T: int) -> list:
+        """The expert kernels run for T tokens (see :func:`kernel_plan`)."""
+        return kernel_plan(self.experts, T * self.k, self.gemm_min_rows)
 
     def buffers(self, T: int) -> _Buffers:
         b = self._bufs.get(T)

@@ -72,6 +72,16 @@ int mb_q8_dequant(const int8_t *q, const void *scales, int scale_f16, int64_t ro
 int mb_gguf_dequant(const uint8_t *raw, int qtype, int64_t rows, int64_t row_bytes, int64_t cols, float *out,
                     void *stream);
 
+/* moelan/kernels.py:981 gguf_matmul_t(x, raw, qtype, cols): x @ W.T straight
+ * from the GGUF blocks of W (rows, row_bytes), for the few input rows of a
+ * decode step (the reference's fused mat-vecs _mv_q8_0 / _mv_q4_k / _mv_q5_k /
+ * _mv_q2_k / _mv_q3_k / _mv_q6_k, kernels.py:482-676, and its row-decoding
+ * _gguf_mm for the other types).  Every type of mb_gguf_dequant; each weight
+ * is decoded bit-exactly, products and sums in f32.  x (n, cols) f32 and
+ * y (n, rows) f32, x 16-byte aligned. */
+int mb_gguf_matmul_t(const uint8_t *raw, int qtype, int64_t rows, int64_t row_bytes, int64_t cols, const float *x,
+                     int64_t n, float *y, void *stream);
+
 /* ---- router ------------------------------------------------------------------ */
 
 /* Workspace bytes of mb_router_logits / mb_router_route. */
@@ -160,9 +170,11 @@ int mb_moe_decode(const MbExpert *table, int E, int H, int I, int gs, int fmt_gu
  * (about 1360 picks at I = 768); larger calls fail with MB_EINVAL.  The
  * call allocates nothing.  The first call on each device looks up the array's
  * device address (cudaGetSymbolAddress); make that first call before any
- * stream capture.  All calls share the one array: calls that overlap on the
- * GPU (other streams, other host threads) race on it and must be ordered by
- * the caller. */
+ * stream capture.  The address is kept for the life of the process, so no
+ * call may follow a reset of the device's context (cudaDeviceReset): the
+ * kept address would then be stale.  All calls share the one array: calls
+ * that overlap on the GPU (other streams, other host threads) race on it and
+ * must be ordered by the caller. */
 int mb_moe_decode_noalloc(const MbExpert *table, int E, int H, int I, int gs, int fmt_gu, int fmt_down,
                           const float *x, const int32_t *row_exp, int64_t T, const int32_t *counts,
                           const int32_t *offsets, const int32_t *sorted_rows, int64_t P, int max_rows, float *y,
@@ -193,7 +205,7 @@ int64_t mb_moe_prefill_workspace_bytes(int64_t P, int H, int I, int fmt_gu);
  * weights whose activations can be heavy-tailed, where f16 operands alone
  * exceed that bar) the gate|up GEMM runs as three f16 products of the
  * weights' and tokens' f16 pieces (hi*hi + hi*lo + lo*hi) summed in f32.
- * Needs H % 128 == 0, I % 64 == 0, P <= 65535, x and workspace 16-byte
+ * Needs H % 128 == 0, I % 64 == 0, P <= 65536, x and workspace 16-byte
  * aligned. */
 int mb_moe_prefill(const MbExpert *table, const int32_t *e_exp, int E, int H, int I, int gs, int fmt_gu,
                    int fmt_down, const float *x, const int32_t *row_exp, int64_t T, const int32_t *counts,

@@ -55,3 +55,17 @@ def test_expert_parallel_slice_decides_by_its_own_picks(monkeypatch):
     assert _run(monkeypatch, ex, 4096, picks=512) == [("decode", 31), ("gemm", 32)]
     assert _run(monkeypatch, ex, 4096, picks=255) == [("decode", 0)]   # below 16 per expert on average
     assert _run(monkeypatch, ex, 16384, picks=2048) == [("gemm", 1)]
+
+
+def test_gemm_only_experts_without_exponents_raise(monkeypatch):
+    # experts stored from raw tiles without the tensor-core exponents cannot run as grouped GEMMs
+    ex = _experts(fmt=L.FMT_Q4K_F32)
+    ex.missing_exp = {3}
+    with pytest.raises(ValueError, match="exponents"):
+        _run(monkeypatch, ex, 1)
+
+
+def test_largest_permutation_reaches_the_gemm(monkeypatch):
+    # mb_permute takes up to 65536 picks and so does the grouped GEMM: T=8192, k=8 on a GEMM-only layer
+    assert _run(monkeypatch, _experts(fmt=L.FMT_Q4K_F32), 65536) == [("gemm", 1)]
+    assert _run(monkeypatch, _experts(), 65536) == [("gemm", 1)]

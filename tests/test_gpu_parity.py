@@ -234,6 +234,31 @@ def test_gguf_q8_0_and_q4_0_matmul(D, golden, rows):
     assert row_err(got, golden[f"gguf_mm_2_{rows}"]) < TOL_F32
 
 
+@pytest.mark.parametrize("qt", sorted(C.GGUF_BLOCK))
+@pytest.mark.parametrize("rows", C.GGUF_MM_ROWS)
+def test_gguf_matmul_all_types(D, golden, qt, rows):
+    """mb_gguf_matmul_t straight from the blocks, every type, against the
+    reference's fused mat-vecs (its own bar: rtol = atol = 1e-4,
+    tests/test_gguf.py:34-39) and against the oracle's f32 product of the
+    bit-exact dequantised weights (1e-5 per row)."""
+    raw, x = C.gguf_mm_inputs(qt, rows)
+    got = D.gguf_matmul_t(cu(raw), qt, C.GGUF_COLS, cu(x)).cpu().numpy()
+    np.testing.assert_allclose(got, golden[f"gguf_mm_{qt}_{rows}"], rtol=1e-4, atol=1e-4)
+    w = O.gguf_dequant(raw, qt, C.GGUF_COLS).astype(np.float64)
+    assert row_err(got, x.astype(np.float64) @ w.T) < TOL_F32
+
+
+@pytest.mark.parametrize("qt", [12, 8, 14])
+def test_gguf_matmul_wide(D, qt):
+    """Mixtral-wide rows (K = 14336) and more input rows than one pass takes."""
+    rng = np.random.default_rng(qt)
+    raw = C.gguf_random_rows(40, 14336, qt, rng, 0.001)
+    x = rng.standard_normal((11, 14336)).astype(np.float32)
+    got = D.gguf_matmul_t(cu(raw), qt, 14336, cu(x)).cpu().numpy()
+    w = O.gguf_dequant(raw, qt, 14336).astype(np.float64)
+    assert row_err(got, x.astype(np.float64) @ w.T) < TOL_F32
+
+
 # ---- one MoE layer ------------------------------------------------------------------
 
 def _layer(cfg, kind, experts, router, f16=False):

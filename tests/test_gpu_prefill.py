@@ -158,6 +158,89 @@ def test_qwen_shape_prefill_layer_matches_oracle(qwen_q8, T):
     assert layer.status(T) == 0
 
 
+@pytest.fixture(scope="module")
+def qwen_q4(D):
+    """The north_star prefill layer: int4 group-32 experts with f16 scales in
+    the Qwen3-30B-A3B layer shape (the benchmark's own recipe)."""
+    from distributedmoellm_b200 import synthetic as S
+    from distributedmoellm_b200.layer import MoELayer
+    rng = np.random.default_rng(5)
+    H, I, E, k, gs = 2048, 768, 128, 8, 32
+    ex, desc = _experts(rng, "q4h", E, H, I, gs)
+    router = S.router(rng, E, H)
+    return MoELayer(cu(router), ex, k, True), desc, router, dict(H=H, I=I, E=E, k=k)
+
+
+@pytest.mark.parametrize("T", [2048, 4096])
+def test_qwen_shape_int4_prefill_layer_matches_oracle(qwen_q4, T):
+    layer, desc, router, cfg = qwen_q4
+    assert layer.uses_gemm(T)
+    from distributedmoellm_b200 import synthetic as S
+    x = S.hidden(np.random.default_rng(300 + T), T, cfg["H"])
+    out = layer(cu(x)).cpu().numpy()
+    b = layer.buffers(T)
+    idx, w = b.idx.cpu().numpy(), b.w.cpu().numpy()
+    ex, off, rows, wts = O.group_by_expert(idx, w)
+    groups = [(ex[i], rows[off[i]:off[i + 1]], wts[off[i]:off[i + 1]]) for i in range(len(ex))]
+    want = O.store_compute(x, groups, desc, cfg["I"])
+    assert row_err(out, want) < TOL_TC
+    assert layer.status(T) == 0
+
+
+def _heavy_tailed(rng, T, H):
+    """N(0, 1) token rows, with some rows far from it: a single large outlier
+    per row, Student-t rows (df 1.5), and whole rows scaled by 1e-3 and 1e3."""
+    x = rng.standard_normal((T, H), dtype=np.float32)
+    n = max(1, T // 16)
+    for r in range(0, n):
+        x[r, rng.integers(0, H)] = np.float32(rng.choice([-1, 1]) * 300.0)
+    x[n:2 * n] = rng.standard_t(1.5, (n, H)).astype(np.float32)
+    x[2 * n:3 * n] *= np.float32(1e-3)
+    x[3 * n:4 * n] *= np.float32(1e3)
+    return x
+
+
+@pytest.mark.parametrize("kind", ["q4h", "q8"])
+def test_prefill_quantised_gaussian_weights_heavy_tailed_tokens(D, kind):
+    """Weights quantised from N(0, 0.02) (int4: symmetric, scale absmax / 7,
+    moelan/tiny.py:94-100, scales through f16; int8: GroupQuant.quantize,
+    moelan/experts.py:134-142) instead of the uniform-nibble benchmark recipe,
+    and heavy-tailed token rows: the activation exponent bound of the
+    tensor-core path keeps the 2e-3 bar outside the synthetic recipe."""
+    import cases as C
+    from distributedmoellm_b200 import layout as L
+    from distributedmoellm_b200 import synthetic as S
+    from distributedmoellm_b200.layer import MoELayer
+    from distributedmoellm_b200.store import LayerExperts
+    rng = np.random.default_rng(61 if kind == "q4h" else 62)
+    H, I, E, k, gs, T = 2048, 768, 16, 2, 32, 1024
+    fmt = L.FMT_Q4_F16 if kind == "q4h" else L.FMT_Q8_F32
+    ex = LayerExperts(E, H, I, gs, fmt, fmt, "cuda")
+    desc = {}
+    for e in range(E):
+        if kind == "q4h":
+            gr, gsc, dr, dsc = C.int4_expert(rng, H, I, gs, f16_scales=True)
+            ex.put_int4(e, gr, gsc.astype(np.float16), dr, dsc.astype(np.float16))
+            desc[e] = (("q4", gr, gsc, gs, False), ("q4", dr, dsc, gs, False))
+        else:
+            gq, gsc, dq, dsc = C.int8_expert(rng, H, I, gs)
+            ex.put_int8(e, gq, gsc, dq, dsc)
+            desc[e] = (("q8", gq, gsc, gs), ("q8", dq, dsc, gs))
+    ex.publish()
+    layer = MoELayer(cu(S.router(rng, E, H)), ex, k, True)
+    assert layer.uses_gemm(T)
+    x = _heavy_tailed(rng, T, H)
+    out = layer(cu(x)).cpu().numpy()
+    b = layer.buffers(T)
+    idx, w = b.idx.cpu().numpy(), b.w.cpu().numpy()
+    e_, off, rows, wts = O.group_by_expert(idx, w)
+    groups = [(e_[i], rows[off[i]:off[i + 1]], wts[off[i]:off[i + 1]]) for i in range(len(e_))]
+    want = O.store_compute(x, groups, desc, I)
+    assert np.isfinite(out).all()
+    assert row_err(out, want) < TOL_TC
+    assert layer.status(T) == 0
+
+
 def test_prefill_repeats_bit_identical(qwen_q8):
     """The grouped GEMMs are deterministic: repeated layer calls (two passes
     per expert at 4096 tokens) give bit-identical outputs and a clean status."""
@@ -209,7 +292,7 @@ def test_gguf_q4_k_layer_matches_oracle(D):
         _check_gguf_layer(layer, desc, rng.standard_normal((T, 512), dtype=np.float32), 256)
 
 
-@pytest.mark.parametrize("T", [1, 16])
+@pytest.mark.parametrize("T", [1, 16, 512])
 def test_gguf_mixtral_shape_matches_oracle(D, T):
     """Config 4: d_model 4096, 8 experts top-2, intermediate 14336, Q4_K gate/up, Q8_0 down."""
     global _MIXTRAL

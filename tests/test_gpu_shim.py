@@ -83,6 +83,26 @@ def test_matmul_entry_points(K, n):
         assert row_err(K.gguf_matmul_t(x, raw, qt, 512), O.gguf_matmul_t(x, raw, qt, 512)) < TOL
 
 
+@pytest.mark.parametrize("qt", [2, 3, 6, 7, 8, 10, 11, 12, 13, 14])
+def test_gguf_matmul_t_takes_every_type(K, qt):
+    """install() puts this in place of moelan.kernels.gguf_matmul_t, which
+    moelan's QuantMatrix.matmul_t calls for every GGUF matrix with fewer than
+    eight input rows (moelan/gguf.py:287-289): no type moelan reads may fail."""
+    import cases as C
+    rng = np.random.default_rng(100 + qt)
+    raw = C.gguf_random_rows(48, 512, qt, rng, 0.01)
+    for n in (1, 5):
+        x = rng.standard_normal((n, 512), dtype=np.float32)
+        w = O.gguf_dequant(raw, qt, 512).astype(np.float64)
+        assert row_err(K.gguf_matmul_t(x, raw, qt, 512), x.astype(np.float64) @ w.T) < TOL
+    # a Mixtral-wide Q8_0 down projection (K = 14336) as well
+    if qt == 8:
+        raw = C.gguf_random_rows(64, 14336, 8, rng, 0.001)
+        x = rng.standard_normal((1, 14336), dtype=np.float32)
+        w = O.gguf_dequant(raw, 8, 14336).astype(np.float64)
+        assert row_err(K.gguf_matmul_t(x, raw, 8, 14336), x.astype(np.float64) @ w.T) < TOL
+
+
 def test_moe_q4_matches_the_reference_kernel(K):
     rng = np.random.default_rng(7)
     H, I, gs, T = 512, 256, 32, 12
