@@ -153,11 +153,22 @@ def measure_prefill(layer, T, steps, warmup, world, dev, seed=5):
         torch.cuda.synchronize()
         return a.elapsed_time(b) / n
 
+    full.replay()
+    check_status([layer], T)
     ms, ex_ms = timed(full, steps), timed(ex, steps)
     st = int(layer.status(T))
     plan = layer.kernel_plan(T)
     del full, ex
     return ms, ex_ms, st, plan
+
+
+def check_status(layers, T):
+    """Stop at once when a kernel reported a failure (a wait that ran out of
+    time sets a status bit and every later wait of that launch gives up), so a
+    broken build does not run its whole timed loop at two seconds a launch."""
+    st = max(int(l.status(T)) for l in layers)
+    if st:
+        raise RuntimeError(f"the expert kernels reported status {st} at T={T}")
 
 
 # ---- clocks sampled during the timed region ------------------------------------------
@@ -449,6 +460,7 @@ def run_gpu(args, rank, world, dev):
         L = len(layers)
         for i in range(warmup):
             full[i % L].replay()
+        check_status(layers, T)
 
         def timed(graphs):
             if world > 1:

@@ -141,6 +141,7 @@ class GpuTier:
         self.busy_s = 0.0
         self.share = 0.0
         self.gpu_ms = self.cpu_ms = None
+        self.gpu_device_ms = None
         self.status = 0
 
     def expert_bytes(self, inter: int, hidden: int) -> int:
@@ -176,13 +177,15 @@ class GpuTier:
         return uniq, part, status, t0
 
     def launch_held(self, layer: int, x: np.ndarray, groups):
-        """Launch those of ``groups`` whose experts this GPU holds; returns
-        (handle or None, the other groups).  Atomic with :meth:`release`."""
+        """Launch the groups whose experts this tier holds and hand back the
+        rest: (handle or None, groups left for the CPU).  The membership test
+        and the launch happen under the tier's lock, so release() cannot
+        empty the tier in between."""
         with self.lock:
-            on = [g for g in groups if (layer, int(g[0])) in self.experts]
-            if not on:
-                return None, groups
-            return self.launch(layer, x, on), [g for g in groups if (layer, int(g[0])) not in self.experts]
+            mine, rest = [], []
+            for g in groups:
+                (mine if (layer, int(g[0])) in self.experts else rest).append(g)
+            return (self.launch(layer, x, mine) if mine else None), rest
 
     def release(self) -> None:
         """Free the GPU's memory; its experts are computed on the CPU from now on."""
@@ -205,34 +208,55 @@ class GpuTier:
             raise RuntimeError(f"GPU expert kernels reported status {st}")
 
     def calibrate(self, sample_expert, cpu_expert_fn, hidden: int, repeats: int = 12) -> float:
-        """Time one expert on each device (1 input row, transfers included) and
-        set ``share`` = cpu / (gpu + cpu), as moelan/accel.py:141-177 does."""
-        if not self.add((-1, 0), sample_expert):
+        """Set ``share``, the fraction of routed work this GPU should take so it
+        and the CPU finish a layer together: share = cpu / (gpu + cpu), from
+        the median wall time per expert of each side on one input row (a
+        decode step), the GPU side through launch + collect with the host
+        copies that a real call makes.  The device time of the GPU side alone
+        (CUDA events) is kept in ``gpu_device_ms``.  The sample expert is
+        uploaded under a key no layer routes to and dropped afterwards."""
+        key = (-1, 0)
+        if not self.add(key, sample_expert):
             raise RuntimeError("the sample expert has no packed form for this GPU tier")
-        x = np.random.default_rng(0).standard_normal((1, hidden)).astype(np.float32)
-        groups = [(0, np.array([0]), np.ones(1, np.float32))]
+        try:
+            x = np.random.default_rng(0).standard_normal((1, hidden)).astype(np.float32)
+            groups = [(0, np.zeros(1, np.int64), np.ones(1, np.float32))]
+            sink = np.zeros_like(x)
 
-        def gpu_once():
-            o = np.zeros_like(x)
-            self.collect(self.launch(-1, x, groups), o)
-        for _ in range(3):
-            gpu_once()
-            cpu_expert_fn(x)
-        t0 = time.perf_counter()
-        for _ in range(repeats):
-            gpu_once()
-        g = (time.perf_counter() - t0) / repeats
-        t0 = time.perf_counter()
-        for _ in range(repeats):
-            cpu_expert_fn(x)
-        c = (time.perf_counter() - t0) / repeats
-        with self.lock:
-            self.experts.pop((-1, 0))
-            self.used -= self.pool.pop((-1, 0))
-        self.calls = 0
-        self.busy_s = 0.0
-        self.gpu_ms, self.cpu_ms = g * 1000, c * 1000
-        self.share = c / (g + c)
+            def on_gpu():
+                self.collect(self.launch(key[0], x, groups), sink)
+
+            def on_cpu():
+                cpu_expert_fn(x)
+
+            def median_s(fn, n):
+                ts = []
+                for _ in range(n):
+                    t0 = time.perf_counter()
+                    fn()
+                    ts.append(time.perf_counter() - t0)
+                return float(np.median(ts))
+
+            n = max(1, int(repeats))
+            median_s(on_gpu, 3)                # first calls: kernel set-up, allocator, page-in
+            median_s(on_cpu, 3)
+            g = median_s(on_gpu, n)
+            c = median_s(on_cpu, n)
+            with torch.cuda.device(self.device):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                self.launch(key[0], x, groups)
+                b.record()
+                b.synchronize()
+                self.gpu_device_ms = a.elapsed_time(b)
+        finally:
+            with self.lock:
+                self.experts.pop(key, None)
+                if key in self.pool.entries:
+                    self.used -= self.pool.pop(key)
+        self.calls, self.busy_s = 0, 0.0          # calibration traffic is not routed work
+        self.gpu_ms, self.cpu_ms = 1e3 * g, 1e3 * c
+        self.share = c / (g + c) if g + c > 0 else 0.0
         return self.share
 
     def stats(self) -> dict:
@@ -243,16 +267,23 @@ class GpuTier:
 
 
 def bench_gpu(spec: str, budget: int, hidden: int, inter: int, fmt: str, gs: int = 64, make_expert=None) -> dict:
-    """GPU side of a node's speed benchmark (moelan/accel.py:400-411): ms per
-    expert on the GPU (one input row, transfers included) and how many experts
-    fit in ``budget``.  ``make_expert(hidden, inter, fmt, gs)`` defaults to
-    moelan.experts.synthetic_expert."""
+    """The GPU half of a node's speed benchmark (what moelan/accel.py:400-411
+    reports): ``gpu_ms``, the wall time per expert of a one-row call on this
+    tier (host copies included), ``gpu_experts``, how many experts of this
+    shape fit in ``budget`` in their packed form on the device, and
+    ``gpu_name``.  ``make_expert(hidden, inter, fmt, gs)`` builds the sample
+    (default moelan.experts.synthetic_expert); the sample's own __call__ is the
+    CPU side of the calibration.  Raises RuntimeError when the device cannot
+    be opened or the sample has no packed form."""
     if make_expert is None:
         from moelan.experts import synthetic_expert as make_expert
+    sample = make_expert(hidden, inter, fmt, gs)
+    packed = pack_expert(sample)
+    if packed is None:
+        raise RuntimeError(f"a {fmt} expert has no packed form for this GPU tier")
     tier = GpuTier(spec, budget)
-    e = make_expert(hidden, inter, fmt, gs)
-    tier.calibrate(e, lambda x: e(x), hidden)
-    out = {"gpu_ms": tier.gpu_ms, "gpu_experts": int(budget // tier.expert_bytes(inter, hidden)),
-           "gpu_name": tier.name}
-    tier.release()
-    return out
+    try:
+        tier.calibrate(sample, sample, hidden)
+        return {"gpu_ms": tier.gpu_ms, "gpu_experts": int(budget // max(1, packed.nbytes)), "gpu_name": tier.name}
+    finally:
+        tier.release()

@@ -8,6 +8,9 @@ static thread_local char g_last_error[512] = "";
 
 int mb_fail(int code, const char* fmt, ...)
 {
+    // a failed CUDA call also leaves its error as the thread's last error: it is
+    // reported here, so clear it (the next call's launch check must not see it)
+    if (code == MB_ECUDA) (void)cudaGetLastError();
     va_list ap;
     va_start(ap, fmt);
     vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);

@@ -40,7 +40,12 @@ inline cudaError_t mb_launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+    // a refused launch also records itself as the thread's last CUDA error; it is
+    // reported through the return value, so clear it here, or the next
+    // mb_check_launch (of an unrelated call) would report it again
+    if (e != cudaSuccess) (void)cudaGetLastError();
+    return e;
 }
 
 #define MB_REQUIRE(cond, ...)                                  \

@@ -28,9 +28,17 @@
 //    activation row (P x I) goes back to HBM, with each pick's max |act|.
 //  * Phase 2 (down) writes each pick's unweighted output row; the weighted
 //    combine is a separate deterministic kernel.
-//  * Work items are (expert, chunk of 8 picks, MT row tiles), split
+//  * Work units are (expert, chunk of 8 picks, MT row tiles), split
 //    contiguously over a persistent grid so each CTA touches one or two
 //    experts.
+//  * K above 2048 (16 MMA warps of one 128-column quad each) is cut into
+//    windows of 16 quads: a CTA walks each segment of its units (up to 32 row
+//    tiles of one chunk) once per window, loading the activation fragments of
+//    the window once per segment, and the epilogue keeps the segment's partial
+//    sums in shared memory until the last window.
+//  * The affine int4 format (GGUF Q4_K as (u - 8) * scale + bias per group of
+//    32) adds bias * (the group's sum of the activations) per group, the sums
+//    formed once per chunk and window from the same scaled activations.
 #include <algorithm>
 #include <type_traits>
 
@@ -38,16 +46,18 @@
 
 namespace {
 
-constexpr int kMaxKW = 16;      // MMA warps: one per quad (128 columns) of K, so K <= 2048
-constexpr int kEpiWarps = 2;    // epilogue warps, taking alternate items
+constexpr int kMaxKW = 16;      // MMA warps: one per quad (128 columns) of a K window of up to 2048 columns
+constexpr int kEpiWarps = 2;    // epilogue warps, taking alternate items (one warp with K windows)
 constexpr int kMaxMT = 4;       // row tiles per stage
 constexpr int kRedTile = 128;   // floats of one warp's partial of one tile: [8 input rows][16 rows]
 constexpr int kMaxCachedE = 1024;  // experts whose weight address the kernel keeps in shared memory
 constexpr int kMaxCachedP = 1024;  // picks whose token row and exponent the kernel keeps in shared memory
+constexpr int kSegTiles = 32;   // K > 2048: row tiles of a segment whose partial sums wait in shared memory
 
 struct Fmt {
     int data_bytes;   // per block: 1024 (int4) or 2048 (int8)
     int scale_f16;    // scale element 2 or 4 bytes
+    int affine;       // int4 with an f32 bias per group after the scales (GGUF Q4_K)
     int block_bytes;
 };
 
@@ -56,7 +66,8 @@ __host__ __device__ inline Fmt fmt_info(int fmt)
     Fmt f;
     f.data_bytes = (fmt == MB_FMT_Q8_F16 || fmt == MB_FMT_Q8_F32) ? 2048 : 1024;
     f.scale_f16 = (fmt == MB_FMT_Q4_F16 || fmt == MB_FMT_Q8_F16) ? 1 : 0;
-    f.block_bytes = f.data_bytes + 16 * 4 * (f.scale_f16 ? 2 : 4);
+    f.affine = fmt == MB_FMT_Q4K_F32;
+    f.block_bytes = f.data_bytes + 16 * 4 * (f.scale_f16 ? 2 : 4) + (f.affine ? 16 * 4 * 4 : 0);
     return f;
 }
 
@@ -66,13 +77,16 @@ struct DecodeArgs {
     int phase;        // 1: gate|up -> act, 2: down -> y
     int K;            // real input columns
     int NQ;           // quads per tile row (K padded to 128)
+    int QW;           // quads per K window (= MMA warps)
+    int NW;           // K windows: one MMA warp per quad of a window, windows one after another
+    int SEG;          // units (stages) of a segment: the partial sums of its tiles wait for the last window
     int RT;           // row tiles
     int MT;           // row tiles per stage
     int O_real;       // phase 1: I (act columns), phase 2: H (y columns)
     int src_ld;       // floats per input row (x: H, act: I_pad)
     int act_ld;       // I_pad
     int y_ld;         // H
-    int KW;           // MMA warps (= NQ)
+    int KW;           // MMA warps (= QW)
     int stages, tile_bytes, nred;
     const int32_t* counts;
     const int32_t* offsets;
@@ -97,14 +111,14 @@ __device__ __forceinline__ int64_t items_of(int n, int max_rows, int RTS)
     return (n > 0 && n <= max_rows) ? (int64_t)((n + 7) >> 3) * RTS : 0;
 }
 
-// Estimated cost of the work, for splitting it over the CTAs: an item of a
-// chunk of at most 4 picks costs kCostOne, of 5..8 picks (both N tiles of the
-// MMAs live) kCostTwo, and the first item of a chunk kCostSwitch more (the
-// chunk's activation rows are gathered from global memory there).  Item
-// weights from per-item timings on B200 (0.94 / 1.18 us per two-tile item);
-// the switch weight is the best of 0, 3, 6, 12 and 20 in timed decode steps
-// (T = 32 and 64): with the rows kept in L2 a switch mostly overlaps the
-// stages already in flight.
+// Estimated cost of the work, for splitting it over the CTAs: a unit (one
+// stage of row tiles over all of K) of a chunk of at most 4 picks costs
+// kCostOne, of 5..8 picks (both N tiles of the MMAs live) kCostTwo, and the
+// first unit of a chunk kCostSwitch more (the chunk's activation rows are
+// gathered from global memory there).  Unit weights from per-unit timings on
+// B200 (0.94 / 1.18 us per two-tile unit); the switch weight is the best of 0,
+// 3, 6, 12 and 20 in timed decode steps (T = 32 and 64): with the rows kept in
+// L2 a switch mostly overlaps the stages already in flight.
 constexpr int kCostOne = 4, kCostTwo = 5, kCostSwitch = 3;
 
 __device__ __forceinline__ int64_t cost_of(int n, int max_rows, int RTS)
@@ -116,7 +130,7 @@ __device__ __forceinline__ int64_t cost_of(int n, int max_rows, int RTS)
            kCostSwitch;
 }
 
-// The first item whose start cost is at least c (pre: item prefix, cpre: cost prefix over experts).
+// The first unit whose start cost is at least c (pre: unit prefix, cpre: cost prefix over experts).
 __device__ int64_t item_at_cost(const int64_t* pre, const int64_t* cpre, const int32_t* cnt, int E, int RTS, int64_t c)
 {
     if (c >= cpre[E]) return pre[E];
@@ -141,7 +155,7 @@ __device__ int64_t item_at_cost(const int64_t* pre, const int64_t* cpre, const i
         rel -= full * tf;
         cc = last > 4 ? kCostTwo : kCostOne;
     }
-    // item 0 of a chunk spans [0, kCostSwitch + cc), item k >= 1 starts at kCostSwitch + k * cc
+    // unit 0 of a chunk spans [0, kCostSwitch + cc), unit k >= 1 starts at kCostSwitch + k * cc
     const int64_t k = rel == 0 ? 0 : max((int64_t)1, (rel - kCostSwitch + cc - 1) / cc);
     return pre[lo] + j * RTS + k;
 }
@@ -190,7 +204,7 @@ __device__ __forceinline__ void scales4(const uint8_t* p, float (&s)[4])
     }
 }
 
-// Work-item cursor over (expert, chunk of 8 picks, stage of MT row tiles).
+// Cursor over the units (expert, chunk of 8 picks, stage of MT row tiles).
 struct ItemCursor {
     int e, c, sg;
     __device__ __forceinline__ void start(const int64_t* pre, int E, int RTS, int64_t item)
@@ -218,60 +232,113 @@ struct ItemCursor {
     }
 };
 
-// One row tile of one MMA warp: its QPW blocks (16 rows x 128 columns) of a
-// tile in shared memory against the activation fragments bf, group
-// scales applied in f32, the partial sums stored to rt ([input row][16 rows]).
-// blk0: the warp's first block of the tile.
-// TWO: the second N tile (input rows 4..7) is live.
-template <bool Q8, bool F16S, int QPW, bool TWO>
-__device__ __forceinline__ void tile_mma(const uint8_t* __restrict__ blk0, int nq, const uint32_t (&bf)[QPW][2][4][4],
-                                         float* __restrict__ rt, int t, int g)
+// Cursor over the work items of one CTA: its run of units is cut into
+// segments (consecutive units of one chunk, at most SEG of them), and each
+// segment is walked once per K window, so the activation fragments of a window
+// are loaded once per segment and the partial sums of a segment's tiles wait in
+// shared memory for the last window.  With one window (K <= 2048) the items are
+// the units themselves, in order.
+struct WinCursor {
+    ItemCursor u, s0;   // the current unit, the segment's first unit
+    int64_t rem;        // units of the run from the segment's first unit on
+    int j, len, w;      // unit within the segment, segment length, window
+    __device__ __forceinline__ void seg_init(int RTS, int SEG)
+    {
+        int64_t l = RTS - u.sg;                 // units left in this chunk
+        if (l > SEG) l = SEG;
+        if (l > rem) l = rem;
+        len = (int)l;
+    }
+    __device__ __forceinline__ void start(const int64_t* pre, int E, int RTS, int SEG, int64_t lo, int64_t hi)
+    {
+        u.start(pre, E, RTS, lo);
+        s0 = u;
+        rem = hi - lo;
+        j = w = 0;
+        seg_init(RTS, SEG);
+    }
+    __device__ __forceinline__ void next(const int64_t* pre, int E, int RTS, int SEG, int NW)
+    {
+        if (++j < len) {
+            u.next(pre, E, RTS);
+            return;
+        }
+        j = 0;
+        if (++w < NW) {
+            u = s0;
+            return;
+        }
+        w = 0;
+        rem -= len;
+        u.next(pre, E, RTS);
+        s0 = u;
+        if (rem > 0) seg_init(RTS, SEG);
+    }
+};
+
+// One row tile of one MMA warp: its block (16 rows x 128 columns) of a tile in
+// shared memory against the activation fragments bf, group scales applied in
+// f32 (and for the affine format the group biases times the rows' group sums
+// xs), the partial sums stored to rt ([input row][16 rows]).  has: the warp's
+// quad exists in this K window (else its partials are zero).  TWO: the second N
+// tile (input rows 4..7) is live.
+template <bool Q8, bool F16S, bool AFF, bool TWO>
+__device__ __forceinline__ void tile_mma(const uint8_t* __restrict__ blk, bool has, const uint32_t (&bf)[2][4][4],
+                                         const float (&xs)[2][4], float* __restrict__ rt, int t, int g)
 {
     constexpr int kData = Q8 ? 2048 : 1024;
-    constexpr int kBlock = kData + 16 * 4 * (F16S ? 2 : 4);
     float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [N tile][row g, row g+8] of input row 4nt + t
+    if (has) {
+        const uint8_t* wp = blk + g * 64 + t * 16;
+        const uint8_t* sp = blk + kData + g * (F16S ? 8 : 16);
+        uint32_t wg[Q8 ? 8 : 4], wh[Q8 ? 8 : 4];
+        {
+            const uint4 a0 = *reinterpret_cast<const uint4*>(wp);
+            const uint4 b0 = *reinterpret_cast<const uint4*>(wp + 8 * 64);
+            wg[0] = a0.x; wg[1] = a0.y; wg[2] = a0.z; wg[3] = a0.w;
+            wh[0] = b0.x; wh[1] = b0.y; wh[2] = b0.z; wh[3] = b0.w;
+        }
+        if (Q8) {
+            const uint4 a1 = *reinterpret_cast<const uint4*>(wp + 1024);
+            const uint4 b1 = *reinterpret_cast<const uint4*>(wp + 1024 + 8 * 64);
+            wg[Q8 ? 4 : 0] = a1.x; wg[Q8 ? 5 : 1] = a1.y; wg[Q8 ? 6 : 2] = a1.z; wg[Q8 ? 7 : 3] = a1.w;
+            wh[Q8 ? 4 : 0] = b1.x; wh[Q8 ? 5 : 1] = b1.y; wh[Q8 ? 6 : 2] = b1.z; wh[Q8 ? 7 : 3] = b1.w;
+        }
+        float sg[4], sh[4], bg[4], bh[4];
+        scales4<F16S>(sp, sg);
+        scales4<F16S>(sp + 8 * (F16S ? 8 : 16), sh);
+        if (AFF) {   // biases follow the 16 x 4 f32 scales
+            scales4<false>(sp + 256, bg);
+            scales4<false>(sp + 256 + 8 * 16, bh);
+        }
 #pragma unroll
-    for (int qi = 0; qi < QPW; ++qi) {
-        if (qi < nq) {
-            const uint8_t* wp = blk0 + qi * kBlock + g * 64 + t * 16;
-            const uint8_t* sp = blk0 + qi * kBlock + kData + g * (F16S ? 8 : 16);
-            uint32_t wg[Q8 ? 8 : 4], wh[Q8 ? 8 : 4];
-            {
-                const uint4 a0 = *reinterpret_cast<const uint4*>(wp);
-                const uint4 b0 = *reinterpret_cast<const uint4*>(wp + 8 * 64);
-                wg[0] = a0.x; wg[1] = a0.y; wg[2] = a0.z; wg[3] = a0.w;
-                wh[0] = b0.x; wh[1] = b0.y; wh[2] = b0.z; wh[3] = b0.w;
-            }
+        for (int gi = 0; gi < 4; ++gi) {
+            uint32_t pg[4], ph_[4];
             if (Q8) {
-                const uint4 a1 = *reinterpret_cast<const uint4*>(wp + 1024);
-                const uint4 b1 = *reinterpret_cast<const uint4*>(wp + 1024 + 8 * 64);
-                wg[Q8 ? 4 : 0] = a1.x; wg[Q8 ? 5 : 1] = a1.y; wg[Q8 ? 6 : 2] = a1.z; wg[Q8 ? 7 : 3] = a1.w;
-                wh[Q8 ? 4 : 0] = b1.x; wh[Q8 ? 5 : 1] = b1.y; wh[Q8 ? 6 : 2] = b1.z; wh[Q8 ? 7 : 3] = b1.w;
+                unpack_q8(wg[(2 * gi) % (Q8 ? 8 : 4)], wg[(2 * gi + 1) % (Q8 ? 8 : 4)], pg);
+                unpack_q8(wh[(2 * gi) % (Q8 ? 8 : 4)], wh[(2 * gi + 1) % (Q8 ? 8 : 4)], ph_);
+            } else {
+                unpack_q4(wg[gi], pg);
+                unpack_q4(wh[gi], ph_);
             }
-            float sg[4], sh[4];
-            scales4<F16S>(sp, sg);
-            scales4<F16S>(sp + 8 * (F16S ? 8 : 16), sh);
-#pragma unroll
-            for (int gi = 0; gi < 4; ++gi) {
-                uint32_t pg[4], ph_[4];
-                if (Q8) {
-                    unpack_q8(wg[(2 * gi) % (Q8 ? 8 : 4)], wg[(2 * gi + 1) % (Q8 ? 8 : 4)], pg);
-                    unpack_q8(wh[(2 * gi) % (Q8 ? 8 : 4)], wh[(2 * gi + 1) % (Q8 ? 8 : 4)], ph_);
-                } else {
-                    unpack_q4(wg[gi], pg);
-                    unpack_q4(wh[gi], ph_);
-                }
-                float d[4];
-                mb_mma_f16_zero(d, pg[0], ph_[0], pg[1], ph_[1], bf[qi][0][gi][0], bf[qi][0][gi][1]);
-                mb_mma_f16(d, pg[2], ph_[2], pg[3], ph_[3], bf[qi][0][gi][2], bf[qi][0][gi][3]);
-                acc[0][0] = fmaf(d[0] + d[1], sg[gi], acc[0][0]);
-                acc[0][1] = fmaf(d[2] + d[3], sh[gi], acc[0][1]);
-                if (TWO) {
-                    float e[4];
-                    mb_mma_f16_zero(e, pg[0], ph_[0], pg[1], ph_[1], bf[qi][1][gi][0], bf[qi][1][gi][1]);
-                    mb_mma_f16(e, pg[2], ph_[2], pg[3], ph_[3], bf[qi][1][gi][2], bf[qi][1][gi][3]);
-                    acc[1][0] = fmaf(e[0] + e[1], sg[gi], acc[1][0]);
-                    acc[1][1] = fmaf(e[2] + e[3], sh[gi], acc[1][1]);
+            float d[4];
+            mb_mma_f16_zero(d, pg[0], ph_[0], pg[1], ph_[1], bf[0][gi][0], bf[0][gi][1]);
+            mb_mma_f16(d, pg[2], ph_[2], pg[3], ph_[3], bf[0][gi][2], bf[0][gi][3]);
+            acc[0][0] = fmaf(d[0] + d[1], sg[gi], acc[0][0]);
+            acc[0][1] = fmaf(d[2] + d[3], sh[gi], acc[0][1]);
+            if (AFF) {
+                acc[0][0] = fmaf(xs[0][gi], bg[gi], acc[0][0]);
+                acc[0][1] = fmaf(xs[0][gi], bh[gi], acc[0][1]);
+            }
+            if (TWO) {
+                float e[4];
+                mb_mma_f16_zero(e, pg[0], ph_[0], pg[1], ph_[1], bf[1][gi][0], bf[1][gi][1]);
+                mb_mma_f16(e, pg[2], ph_[2], pg[3], ph_[3], bf[1][gi][2], bf[1][gi][3]);
+                acc[1][0] = fmaf(e[0] + e[1], sg[gi], acc[1][0]);
+                acc[1][1] = fmaf(e[2] + e[3], sh[gi], acc[1][1]);
+                if (AFF) {
+                    acc[1][0] = fmaf(xs[1][gi], bg[gi], acc[1][0]);
+                    acc[1][1] = fmaf(xs[1][gi], bh[gi], acc[1][1]);
                 }
             }
         }
@@ -282,33 +349,38 @@ __device__ __forceinline__ void tile_mma(const uint8_t* __restrict__ blk0, int n
     rt[(4 + t) * 16 + g + 8] = acc[1][1];
 }
 
-// Warp roles: [0, KW) MMA warps (warp w owns quads QPW*w .. QPW*w+QPW-1 of K), KW the TMA
-// producer, KW+1 and KW+2 the epilogue (even and odd items).  Shared memory:
-// weight stages | reduction buffers [nred][KW][MT][8][16] | mbarriers | item
-// prefix | abort flag.
-// largest block of an instantiation: 16 MMA warps with one quad each, 8 with two
-constexpr int threads_max(int qpw) { return ((qpw == 2 ? kMaxKW / 2 : kMaxKW) + 1 + kEpiWarps) * 32; }
+// Warp roles: [0, KW) MMA warps (warp w owns quad w of the current K window),
+// KW the TMA producer, KW+1 and KW+2 the epilogue (alternate items; with K
+// windows the first takes every item).  Shared memory: weight stages | reduction buffers [nred][KW][MT][8][16]
+// | segment sums [SEG * MT][8][16] (K > 2048 only) | mbarriers | unit prefix |
+// abort flag.
+constexpr int kThreadsMax = (kMaxKW + 1 + kEpiWarps) * 32;
 
-template <int FMT, int QPW>
-__global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const __grid_constant__ DecodeArgs a)
+template <int FMT>
+__global__ void __launch_bounds__(kThreadsMax, 1) moe_decode_kernel(const __grid_constant__ DecodeArgs a)
 {
     constexpr bool Q8 = (FMT == MB_FMT_Q8_F16 || FMT == MB_FMT_Q8_F32);
     constexpr bool F16S = (FMT == MB_FMT_Q4_F16 || FMT == MB_FMT_Q8_F16);
+    constexpr bool AFF = FMT == MB_FMT_Q4K_F32;
     constexpr int kData = Q8 ? 2048 : 1024;
-    constexpr int kBlock = kData + 16 * 4 * (F16S ? 2 : 4);
+    constexpr int kBlock = kData + 16 * 4 * (F16S ? 2 : 4) + (AFF ? 16 * 4 * 4 : 0);
 
     const int S = a.stages, KW = a.KW, E = a.E, RT = a.RT, MT = a.MT, NR = a.nred;
+    const int NW = a.NW, QW = a.QW, NQ = a.NQ, SEG = a.SEG;
     const int RTS = (RT + MT - 1) / MT;
-    const int tile_bytes = a.tile_bytes, stage_bytes = MT * tile_bytes;
+    const int tile_bytes = a.tile_bytes;      // one row tile over all of K in global memory
+    const int wt_bytes = QW * kBlock;         // one row tile over one K window in a stage
+    const int stage_bytes = MT * wt_bytes;
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* stages = smem;
     float* red = reinterpret_cast<float*>(smem + (size_t)S * stage_bytes);
     const int red_buf = KW * MT * kRedTile;  // floats per reduction buffer
-    uint64_t* full = reinterpret_cast<uint64_t*>(red + NR * red_buf);
+    float* segsum = red + NR * red_buf;                                   // [SEG * MT][kRedTile] when NW > 1
+    uint64_t* full = reinterpret_cast<uint64_t*>(segsum + (NW > 1 ? SEG * MT * kRedTile : 0));
     uint64_t* empty = full + S;
     uint64_t* rfull = empty + S;
     uint64_t* rempty = rfull + NR;
-    int64_t* pre = reinterpret_cast<int64_t*>(rempty + NR);  // [E+1] items before expert e
+    int64_t* pre = reinterpret_cast<int64_t*>(rempty + NR);  // [E+1] units before expert e
     int64_t* cpre = pre + E + 1;                                // [E+1] their cost
     const uint8_t** wptr_s = reinterpret_cast<const uint8_t**>(cpre + E + 1);  // [E] when E <= kMaxCachedE
     int32_t* cnt_s = reinterpret_cast<int32_t*>(wptr_s + (E <= kMaxCachedE ? E : 0));  // [E] picks per expert
@@ -338,7 +410,7 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
                 a.single_w ? a.single_w : (a.phase == 1 ? a.table[e].gu : a.table[e].down));
     }
     __syncthreads();
-    if (warp == 0) {  // items and costs per expert -> prefixes
+    if (warp == 0) {  // units and costs per expert -> prefixes
         int64_t run = 0, crun = 0;
         for (int base = 0; base < E; base += 32) {
             const int e = base + lane;
@@ -377,7 +449,7 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
     }
     __syncthreads();
 
-    // this CTA's contiguous run of items: an equal share of the estimated cost
+    // this CTA's contiguous run of units: an equal share of the estimated cost
     const int64_t ctotal = cpre[E];
     const int64_t lo = item_at_cost(pre, cpre, cnt_s, E, RTS, ctotal * blockIdx.x / gridDim.x);
     const int64_t hi = item_at_cost(pre, cpre, cnt_s, E, RTS, ctotal * (blockIdx.x + 1) / gridDim.x);
@@ -386,9 +458,9 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
         if (a.phase == 2) mb_pdl_wait();
         return;
     }
-    const int64_t n_items = hi - lo;
-    ItemCursor cur;
-    cur.start(pre, E, RTS, lo);
+    const int64_t n_items = (hi - lo) * NW;
+    WinCursor cur;
+    cur.start(pre, E, RTS, SEG, lo, hi);
 
     // the picks' rows and exponents, filled by the MMA and epilogue warps while the
     // producer starts the first weight copies (named barrier 1 excludes the producer)
@@ -415,20 +487,31 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
             uint32_t ph = 0;
             int we = -1;
             const uint8_t* wbase = nullptr;
-            for (int64_t it = 0; it < n_items; ++it, cur.next(pre, E, RTS)) {
+            for (int64_t it = 0; it < n_items; ++it, cur.next(pre, E, RTS, SEG, NW)) {
                 if (it >= S && !mb_mbar_wait(&empty[s], ph ^ 1u, a.status, abort_flag)) break;
-                if (cur.e != we) {
-                    we = cur.e;
+                if (cur.u.e != we) {
+                    we = cur.u.e;
                     wbase = E <= kMaxCachedE ? wptr_s[we]
                                              : reinterpret_cast<const uint8_t*>(
                                                    a.single_w ? a.single_w
                                                               : (a.phase == 1 ? a.table[we].gu : a.table[we].down));
                 }
-                const int nt = min(MT, RT - cur.sg * MT);
-                const uint32_t bytes = (uint32_t)(nt * tile_bytes);
-                mb_mbar_arrive_expect_tx(&full[s], bytes);
-                mb_bulk_g2s_hint(stages + (size_t)s * stage_bytes, wbase + (int64_t)cur.sg * MT * tile_bytes, bytes,
-                                 &full[s], wpol);   // weights are read once: the token rows stay in L2
+                const int nt = min(MT, RT - cur.u.sg * MT);
+                uint8_t* dst = stages + (size_t)s * stage_bytes;
+                const uint8_t* src = wbase + (int64_t)cur.u.sg * MT * tile_bytes;
+                if (NW == 1) {   // the stage's tiles are contiguous: one copy
+                    const uint32_t bytes = (uint32_t)(nt * tile_bytes);
+                    mb_mbar_arrive_expect_tx(&full[s], bytes);
+                    mb_bulk_g2s_hint(dst, src, bytes, &full[s], wpol);   // weights are read once: rows stay in L2
+                } else {         // one copy per tile: the window's blocks of each tile
+                    const int qn = min(QW, NQ - cur.w * QW);
+                    const uint32_t wb = (uint32_t)(qn * kBlock);
+                    mb_mbar_arrive_expect_tx(&full[s], wb * (uint32_t)nt);
+                    src += (int64_t)cur.w * QW * kBlock;
+                    for (int mt = 0; mt < nt; ++mt)
+                        mb_bulk_g2s_hint(dst + (size_t)mt * wt_bytes, src + (int64_t)mt * tile_bytes, wb, &full[s],
+                                         wpol);
+                }
                 if (++s == S) {
                     s = 0;
                     ph ^= 1u;
@@ -440,25 +523,36 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
 
     // ------------------------------------------------------------- epilogue
     if (warp > KW) {
-        const int which = warp - KW - 1;    // items it with it % kEpiWarps == which
+        // Which items this warp takes.  One K window: alternate items (it % kEpiWarps), so each reduction
+        // slot (NR a multiple of kEpiWarps) always goes to the same warp, which therefore never waits on a
+        // slot whose earlier item another warp has yet to take.  Several windows: the windows of a unit
+        // must meet in one warp's segment sums, so the first epilogue warp takes every item.
+        const int which = warp - KW - 1;
+        if (NW > 1 && which != 0) return;
         const int n = lane >> 2, rg = lane & 3;  // this lane: input row n, tile rows 4rg..4rg+3
         int ke = -1, kc = -1, pbase = 0, nvalid = 0;
         float fs = 1.f;     // 2^-e of input row n
         float rmax = 0.f;   // phase 1: running max |act| of input row n
-        int r = which;
-        uint32_t rph = 0;
+        int rnext = 0;      // the ring slot of the next item and its phase
+        uint32_t rphn = 0;
         auto flush = [&]() {
             float m = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 1));
             m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
             if (rg == 0 && n < nvalid) atomicMax(&a.act_max[pbase + n], __float_as_uint(m));
             rmax = 0.f;
         };
-        for (int64_t it = 0; it < n_items; ++it, cur.next(pre, E, RTS)) {
-            if ((int)(it & (kEpiWarps - 1)) != which) continue;
-            if (cur.e != ke || cur.c != kc) {
+        for (int64_t it = 0; it < n_items; ++it, cur.next(pre, E, RTS, SEG, NW)) {
+            const int r = rnext;
+            const uint32_t rph = rphn;
+            if (++rnext == NR) {
+                rnext = 0;
+                rphn ^= 1u;
+            }
+            if (NW == 1 && (int)(it & (kEpiWarps - 1)) != which) continue;
+            if (cur.u.e != ke || cur.u.c != kc) {
                 if (a.phase == 1 && ke >= 0) flush();
-                ke = cur.e;
-                kc = cur.c;
+                ke = cur.u.e;
+                kc = cur.u.c;
                 pbase = off_s[ke] + 8 * kc;
                 nvalid = min(8, cnt_s[ke] - 8 * kc);
                 int ex = 0;
@@ -470,7 +564,7 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
                 fs = pow2f(-ex);
             }
             const bool ok = mb_mbar_wait(&rfull[r], rph, a.status, abort_flag);
-            const int nt = min(MT, RT - cur.sg * MT);
+            const int nt = min(MT, RT - cur.u.sg * MT);
             if (ok) {
                 const float* rr = red + r * red_buf;
                 for (int mt = 0; mt < nt; ++mt) {
@@ -483,7 +577,21 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
                         v.z += u.z;
                         v.w += u.w;
                     }
-                    const int rt = cur.sg * MT + mt;
+                    if (NW > 1) {   // the sums over earlier windows wait in shared memory
+                        float4* sp = reinterpret_cast<float4*>(segsum + (cur.j * MT + mt) * kRedTile + n * 16 + 4 * rg);
+                        if (cur.w > 0) {
+                            const float4 q = *sp;
+                            v.x += q.x;
+                            v.y += q.y;
+                            v.z += q.z;
+                            v.w += q.w;
+                        }
+                        if (cur.w + 1 < NW) {
+                            *sp = v;
+                            continue;
+                        }
+                    }
+                    const int rt = cur.u.sg * MT + mt;
                     if (a.phase == 1) {
                         // lanes rg 0,1 hold gate rows 4rg..4rg+3, lanes rg 2,3 the matching up rows
                         const float ux = __shfl_down_sync(0xffffffffu, v.x, 2), uy = __shfl_down_sync(0xffffffffu, v.y, 2);
@@ -514,11 +622,6 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
             }
             __syncwarp();
             if (lane == 0) mb_mbar_arrive(&rempty[r]);
-            r += kEpiWarps;
-            if (r >= NR) {
-                r -= NR;
-                rph ^= 1u;
-            }
         }
         if (a.phase == 1 && ke >= 0) flush();
         return;
@@ -531,27 +634,29 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
     // than 4 picks.  For group column c = 8t + j (j = 0..7), mma 0 takes
     // j in {0, 4 | 1, 5} and mma 1 takes j in {2, 6 | 3, 7} (K slots 2t, 2t+1 |
     // 2t+8, 2t+9), which is the order unpack_q4 / unpack_q8 produce.
-    const int q0 = warp * QPW;  // this warp's first quad of K
-    const int nq = min(QPW, a.NQ - q0);
     const int K = a.K;
-    uint32_t bf[QPW][2][4][4];  // [quad][N tile][group][mma 0 b0, b1, mma 1 b0, b1]
-    int ke = -1, kc = -1;
-    bool two = false;
+    uint32_t bf[2][4][4];  // [N tile][group][mma 0 b0, b1, mma 1 b0, b1]
+    float xs[2][4];        // affine format: group sums of input row 4nt + t (scaled like the pieces)
+    int ke = -1, kc = -1, kw = -1;
+    bool two = false, has = false;
     int s = 0, r = 0;
     uint32_t ph = 0, rph = 0;
-    for (int64_t it = 0; it < n_items; ++it, cur.next(pre, E, RTS)) {
-        if (cur.e != ke || cur.c != kc) {
-            ke = cur.e;
-            kc = cur.c;
+    for (int64_t it = 0; it < n_items; ++it, cur.next(pre, E, RTS, SEG, NW)) {
+        if (cur.u.e != ke || cur.u.c != kc || cur.w != kw) {
+            ke = cur.u.e;
+            kc = cur.u.c;
+            kw = cur.w;
             const int pbase = off_s[ke] + 8 * kc;
             const int nvalid = min(8, cnt_s[ke] - 8 * kc);
+            const int qg = kw * QW + warp;   // this warp's quad of K
             two = nvalid > 4;
+            has = qg < NQ;
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt) {
                 // this lane supplies N slot g: input row 4nt + (g >> 1), piece g & 1
                 const int xr = 4 * nt + (g >> 1);
                 const bool lo_piece = g & 1;
-                const bool valid = xr < nvalid;
+                const bool valid = xr < nvalid && has;
                 const float* src = nullptr;
                 float up = 1.0f;
                 if (valid) {
@@ -568,50 +673,54 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
                     up = pow2f(ex);
                 }
 #pragma unroll
-                for (int qi = 0; qi < QPW; ++qi) {
+                for (int gi = 0; gi < 4; ++gi) {
+                    float v[8];
+                    const int col0 = (qg * 4 + gi) * 32 + 8 * t;
+                    if (valid && col0 + 8 <= K) {
+                        const float4 u0 = *reinterpret_cast<const float4*>(src + col0);
+                        const float4 u1 = *reinterpret_cast<const float4*>(src + col0 + 4);
+                        v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
+                        v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
+                    } else {
 #pragma unroll
-                    for (int gi = 0; gi < 4; ++gi) {
-                        float v[8];
-                        const int col0 = ((q0 + qi) * 4 + gi) * 32 + 8 * t;
-                        if (valid && qi < nq && col0 + 8 <= K) {
-                            const float4 u0 = *reinterpret_cast<const float4*>(src + col0);
-                            const float4 u1 = *reinterpret_cast<const float4*>(src + col0 + 4);
-                            v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
-                            v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
-                        } else {
+                        for (int j = 0; j < 8; ++j) v[j] = (valid && col0 + j < K) ? src[col0 + j] : 0.0f;
+                    }
+                    __half pc[8];
+                    float sum = 0.0f;
 #pragma unroll
-                            for (int j = 0; j < 8; ++j) v[j] = (valid && qi < nq && col0 + j < K) ? src[col0 + j] : 0.0f;
-                        }
-                        __half pc[8];
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            const float xs = v[j] * up;
-                            const __half h = __float2half_rn(xs);
-                            pc[j] = lo_piece ? __float2half_rn(xs - __half2float(h)) : h;
-                        }
-                        bf[qi][nt][gi][0] = mb_pack_h2(pc[0], pc[4]);
-                        bf[qi][nt][gi][1] = mb_pack_h2(pc[1], pc[5]);
-                        bf[qi][nt][gi][2] = mb_pack_h2(pc[2], pc[6]);
-                        bf[qi][nt][gi][3] = mb_pack_h2(pc[3], pc[7]);
+                    for (int j = 0; j < 8; ++j) {
+                        const float xsc = v[j] * up;
+                        const __half h = __float2half_rn(xsc);
+                        pc[j] = lo_piece ? __float2half_rn(xsc - __half2float(h)) : h;
+                        sum += xsc;
+                    }
+                    bf[nt][gi][0] = mb_pack_h2(pc[0], pc[4]);
+                    bf[nt][gi][1] = mb_pack_h2(pc[1], pc[5]);
+                    bf[nt][gi][2] = mb_pack_h2(pc[2], pc[6]);
+                    bf[nt][gi][3] = mb_pack_h2(pc[3], pc[7]);
+                    if (AFF) {
+                        // the 32-column group sum of input row xr (lanes t of this g hold its four 8-column
+                        // parts), then lane (g, t) takes the sum of input row 4nt + t from lane 8t (g = 2t)
+                        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+                        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+                        xs[nt][gi] = __shfl_sync(0xffffffffu, sum, 8 * t);
                     }
                 }
             }
         }
 
-        const int ntiles = min(MT, RT - cur.sg * MT);
+        const int ntiles = min(MT, RT - cur.u.sg * MT);
         if (it >= NR) mb_mbar_wait(&rempty[r], rph ^ 1u, a.status, abort_flag);
         const bool ok = mb_mbar_wait(&full[s], ph, a.status, abort_flag);
         float* rb = red + r * red_buf + warp * MT * kRedTile;
         if (ok) {
-            const uint8_t* stage = stages + (size_t)s * stage_bytes;
+            const uint8_t* stage = stages + (size_t)s * stage_bytes + warp * kBlock;
             if (two) {
                 for (int mt = 0; mt < ntiles; ++mt)
-                    tile_mma<Q8, F16S, QPW, true>(stage + mt * tile_bytes + q0 * kBlock, nq, bf,
-                                                  rb + mt * kRedTile, t, g);
+                    tile_mma<Q8, F16S, AFF, true>(stage + mt * wt_bytes, has, bf, xs, rb + mt * kRedTile, t, g);
             } else {
                 for (int mt = 0; mt < ntiles; ++mt)
-                    tile_mma<Q8, F16S, QPW, false>(stage + mt * tile_bytes + q0 * kBlock, nq, bf,
-                                                   rb + mt * kRedTile, t, g);
+                    tile_mma<Q8, F16S, AFF, false>(stage + mt * wt_bytes, has, bf, xs, rb + mt * kRedTile, t, g);
             }
         } else {
             for (int mt = 0; mt < ntiles; ++mt) {
@@ -636,46 +745,47 @@ __global__ void __launch_bounds__(threads_max(QPW), 1) moe_decode_kernel(const _
 }
 
 struct Cfg {
-    int KW, NQ, QPW, MT, stages, tile_bytes, nred, pc;
+    int KW, NQ, QW, NW, SEG, MT, stages, tile_bytes, nred, pc;
     size_t smem;
 };
 
-#ifndef MB_DECODE_QPW_MIN_NQ
-#define MB_DECODE_QPW_MIN_NQ 99  // two quads per MMA warp from this many quads of K (measured slower: off)
-#endif
-
-// Stage = MT row tiles of ~32 KB; as many stages as fit in the shared memory
-// of one CTA per SM (many MMA warps) or of two (few MMA warps: short K).
+// Stage = MT row tiles (of one K window) of ~32 KB; as many stages as fit in
+// the shared memory of one CTA per SM (many MMA warps) or of two (few MMA
+// warps: short K).  K above 2048 is cut into windows of 16 quads.
 Cfg plan(int fmt, int K, int E, int RT, int P, int phase)
 {
     Cfg c;
     const Fmt f = fmt_info(fmt);
     c.NQ = (K + 127) / 128;
-    c.QPW = c.NQ >= MB_DECODE_QPW_MIN_NQ ? 2 : 1;
-    c.KW = (c.NQ + c.QPW - 1) / c.QPW;
+    c.KW = c.NQ < kMaxKW ? c.NQ : kMaxKW;
+    c.QW = c.KW;
+    c.NW = (c.NQ + c.QW - 1) / c.QW;
     c.tile_bytes = c.NQ * f.block_bytes;
-    c.MT = (32 * 1024 + c.tile_bytes / 2) / c.tile_bytes;
+    const int wt = c.QW * f.block_bytes;
+    c.MT = (32 * 1024 + wt / 2) / wt;
     c.MT = c.MT < 1 ? 1 : (c.MT > kMaxMT ? kMaxMT : c.MT);
     if (c.MT > RT) c.MT = RT < 1 ? 1 : RT;
+    c.SEG = c.NW > 1 ? (kSegTiles / c.MT > 0 ? kSegTiles / c.MT : 1) : (1 << 30);
     // reduction buffers: with many MMA warps each epilogue warp keeps two items in
     // hand (the MMA warps run further ahead); with few, shared memory goes to stages
     c.nred = c.KW > 8 ? 2 * kEpiWarps : kEpiWarps;
     // one CTA per SM with many MMA warps, two with few (113 KB each leaves the per-CTA reserve)
     const size_t budget = c.KW <= 8 ? 113 * 1024 : 220 * 1024;
     const size_t red = (size_t)c.nred * c.KW * c.MT * kRedTile * sizeof(float);
+    const size_t seg = c.NW > 1 ? (size_t)c.SEG * c.MT * kRedTile * sizeof(float) : 0;
     const size_t cache = 2 * (size_t)(E + 1) * sizeof(int64_t) + (E <= kMaxCachedE ? (size_t)E * sizeof(void*) : 0) +
                          2 * (size_t)E * sizeof(int32_t);
-    const size_t stage = (size_t)c.MT * c.tile_bytes;
+    const size_t stage = (size_t)c.MT * wt;
     auto stages_for = [&](size_t fixed) {
         const int st = budget > fixed ? (int)((budget - fixed) / stage) : 2;
         return st < 2 ? 2 : (st > 8 ? 8 : st);
     };
-    const size_t fixed = red + cache + 64 + 16 * sizeof(uint64_t);
+    const size_t fixed = red + seg + cache + 64 + 16 * sizeof(uint64_t);
     // the picks' rows and exponents go to shared memory only where that costs no weight stage
     const size_t pcache = P <= kMaxCachedP ? (phase == 1 ? 2 : 1) * (size_t)P * sizeof(int32_t) : 0;
     c.stages = stages_for(fixed);
     c.pc = (pcache && stages_for(fixed + pcache) == c.stages) ? P : 0;
-    c.smem = (size_t)c.stages * stage + red + (size_t)(2 * c.stages + 2 * c.nred) * sizeof(uint64_t) + cache +
+    c.smem = (size_t)c.stages * stage + red + seg + (size_t)(2 * c.stages + 2 * c.nred) * sizeof(uint64_t) + cache +
              (c.pc ? pcache : 0) + 16;
     return c;
 }
@@ -685,11 +795,11 @@ int launch_phase(const DecodeArgs& base, int K, int RT, cudaStream_t st)
 {
     DecodeArgs a = base;
     const Cfg c = plan(FMT, K, a.E, RT, a.P, a.phase);
-    if (c.KW * 32 + (1 + kEpiWarps) * 32 > threads_max(c.QPW))
-        return mb_fail(MB_EUNSUPPORTED, "mb_moe_decode: K=%d needs %d MMA warps (max %d)", K, c.KW,
-                       threads_max(c.QPW) / 32 - 1 - kEpiWarps);
     a.K = K;
     a.NQ = c.NQ;
+    a.QW = c.QW;
+    a.NW = c.NW;
+    a.SEG = c.SEG;
     a.RT = RT;
     a.MT = c.MT;
     a.KW = c.KW;
@@ -697,7 +807,7 @@ int launch_phase(const DecodeArgs& base, int K, int RT, cudaStream_t st)
     a.tile_bytes = c.tile_bytes;
     a.nred = c.nred;
     a.PC = c.pc;
-    auto kern = c.QPW == 2 ? moe_decode_kernel<FMT, 2> : moe_decode_kernel<FMT, 1>;
+    auto kern = moe_decode_kernel<FMT>;
     const int threads = (c.KW + 1 + kEpiWarps) * 32;
     // one-time per (device, kernel, configuration): raise the shared-memory
     // limit and look up the occupancy, so later calls (and graph captures) only
@@ -705,7 +815,7 @@ int launch_phase(const DecodeArgs& base, int K, int RT, cudaStream_t st)
     struct Occ {
         int dev, threads;
         size_t smem;
-        int per_sm, qpw;
+        int per_sm;
     };
     static thread_local Occ cache[16];
     static thread_local int ncache = 0;
@@ -713,21 +823,24 @@ int launch_phase(const DecodeArgs& base, int K, int RT, cudaStream_t st)
     cudaGetDevice(&dev);
     int per_sm = -1;
     for (int i = 0; i < ncache; ++i)
-        if (cache[i].dev == dev && cache[i].threads == threads && cache[i].smem == c.smem && cache[i].qpw == c.QPW)
-            per_sm = cache[i].per_sm;
+        if (cache[i].dev == dev && cache[i].threads == threads && cache[i].smem == c.smem) per_sm = cache[i].per_sm;
     // the shared-memory limit is an attribute of the kernel, shared by every
     // configuration that launches it: only ever raise it
-    static thread_local size_t smem_attr[2][64] = {{0}};
-    const int di = dev & 63, ki = c.QPW - 1;
-    if (smem_attr[ki][di] < c.smem) {
+    static thread_local size_t smem_attr[64] = {0};
+    const int di = dev & 63;
+    if (smem_attr[di] < c.smem) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem);
-        if (e != cudaSuccess) return mb_fail(MB_ECUDA, "mb_moe_decode: smem attribute: %s", cudaGetErrorString(e));
-        smem_attr[ki][di] = c.smem;
+        if (e != cudaSuccess) {
+            (void)cudaGetLastError();
+            return mb_fail(MB_ECUDA, "mb_moe_decode: smem attribute: %s", cudaGetErrorString(e));
+        }
+        smem_attr[di] = c.smem;
     }
     if (per_sm < 0) {
         cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, c.smem);
+        if (e != cudaSuccess) (void)cudaGetLastError();
         if (e != cudaSuccess || per_sm < 1) per_sm = 1;
-        if (ncache < 16) cache[ncache++] = Occ{dev, threads, c.smem, per_sm, c.QPW};
+        if (ncache < 16) cache[ncache++] = Occ{dev, threads, c.smem, per_sm};
     }
     const int grid = mb_num_sms() * per_sm;
     const cudaError_t le = mb_launch_pdl(kern, dim3(grid), dim3(threads), c.smem, st, a);
@@ -743,6 +856,7 @@ int dispatch_fmt(int fmt, F&& f)
     case MB_FMT_Q4_F16: return f(std::integral_constant<int, MB_FMT_Q4_F16>());
     case MB_FMT_Q8_F32: return f(std::integral_constant<int, MB_FMT_Q8_F32>());
     case MB_FMT_Q8_F16: return f(std::integral_constant<int, MB_FMT_Q8_F16>());
+    case MB_FMT_Q4K_F32: return f(std::integral_constant<int, MB_FMT_Q4K_F32>());
     default: return mb_fail(MB_EUNSUPPORTED, "mb_moe_decode: weight format %d", fmt);
     }
 }

@@ -787,7 +787,10 @@ int launch(const PrefillArgs& a, const TokenMaps& maps, cudaStream_t st)
     cudaGetDevice(&dev);
     if (set[dev & 63] < smem) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return mb_fail(MB_ECUDA, "mb_moe_prefill: smem attribute: %s", cudaGetErrorString(e));
+        if (e != cudaSuccess) {
+            (void)cudaGetLastError();
+            return mb_fail(MB_ECUDA, "mb_moe_prefill: smem attribute: %s", cudaGetErrorString(e));
+        }
         set[dev & 63] = smem;
     }
     const int items = a.E * a.MB;

@@ -36,9 +36,6 @@ _CACHE_MAX = 512
 _lock = threading.RLock()                 # guards the caches below and each call's use of them
 _mats: OrderedDict = OrderedDict()        # matrix key -> (device tiles or raw blocks, fmt, O, K, kept arrays)
 _pool: dict = {}                          # device index -> (DevicePool of moe_q4 experts, their keys in use order)
-# the decode mat-vec kernel on the tile layout takes K up to this; wider GGUF
-# matrices go through the raw-block kernel
-_TILE_MAX_K = 2048
 
 
 def _dev():
@@ -114,11 +111,11 @@ def q8_matmul_t(x: np.ndarray, q: np.ndarray, s: np.ndarray, gs: int) -> np.ndar
 
 def gguf_matmul_t(x: np.ndarray, raw: np.ndarray, qtype: int, cols: int) -> np.ndarray:
     """x @ W.T for GGUF blocks of any type moelan reads (moelan/kernels.py:981-998):
-    Q8_0 and Q4_0 up to K = 2048 as int8 / int4 tiles with their f16 block scales
-    (the tensor-core mat-vec), every other case straight from the blocks
-    (mb_gguf_matmul_t)."""
+    Q8_0 and Q4_0 as int8 / int4 tiles with their f16 block scales (the
+    tensor-core mat-vec, mb_matmul_t), the other types straight from the
+    blocks (mb_gguf_matmul_t)."""
     qtype = int(qtype)
-    if qtype in (8, 2) and cols <= _TILE_MAX_K:
+    if qtype in (8, 2):
         if qtype == 8:
             def make():
                 q, d = layout.q8_0_as_q8(raw, cols)

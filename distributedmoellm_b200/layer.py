@@ -26,23 +26,13 @@ def uses_gemm(experts: LayerExperts, P: int, gemm_min_rows: int) -> bool:
             and P <= 65536 and not experts.missing_exp)
 
 
-def gemm_only(experts) -> bool:
-    """Experts the decode kernels cannot take (the affine int4 format of GGUF
-    Q4_K, or K > 2048 in either matrix) run as grouped GEMMs at any batch size."""
-    from .layout import FMT_Q4K_F32
-    return (FMT_Q4K_F32 in (experts.fmt_gu, experts.fmt_down) or experts.H > 2048 or experts.I > 2048)
-
-
 def kernel_plan(experts, P: int, gemm_min_rows: int) -> list:
     """Which kernels run for P picks over these experts, in launch order:
-    ("decode", max_rows) and / or ("gemm", min_rows).  Experts the decode
-    kernels cannot take always run as grouped GEMMs; otherwise the GEMM runs
-    only for prefill-sized batches (see uses_gemm), over every expert once the
-    picks average twice gemm_min_rows (the decode launches would mostly find
-    nothing to do), else over the experts with at least gemm_min_rows picks
-    with the rest on the decode kernels."""
-    if gemm_only(experts):
-        return [("gemm", 1)]
+    ("decode", max_rows) and / or ("gemm", min_rows).  The GEMM runs only for
+    prefill-sized batches (see uses_gemm), over every expert once the picks
+    average twice gemm_min_rows (the decode launches would mostly find nothing
+    to do), else over the experts with at least gemm_min_rows picks with the
+    rest on the decode kernels."""
     if uses_gemm(experts, P, gemm_min_rows):
         if P >= 2 * experts.E * gemm_min_rows:
             return [("gemm", 1)]
@@ -60,10 +50,6 @@ def run_experts(experts: LayerExperts, x: torch.Tensor, row_exp: torch.Tensor, r
     covers other ranks' experts too), for the choice of kernels."""
     ex, P = experts, routing.P
     plan = kernel_plan(ex, P if picks is None else picks, gemm_min_rows)
-    if gemm_only(ex) and ex.missing_exp:
-        raise ValueError(f"experts {sorted(ex.missing_exp)[:8]} were stored without the exponents the "
-                         f"grouped GEMM needs (put_tiles(..., eexp=None)), and this layer's format or size "
-                         f"(fmt_gu={ex.fmt_gu}, H={ex.H}, I={ex.I}) runs only as grouped GEMMs")
     for kind, rows in plan:
         if kind == "decode":
             D.moe_decode(ex.table, ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down, x, row_exp, routing, y,

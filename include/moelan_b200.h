@@ -44,7 +44,7 @@ enum {
     MB_FMT_Q8_F32 = 3, /* int8, group scales f32 */
     MB_FMT_Q8_F16 = 4, /* int8, group scales f16 (also GGUF Q8_0 blocks) */
     MB_FMT_Q4K_F32 = 5 /* int4 u with value (u - 8) * scale + bias, f32 scales and biases per group of 32
-                          (GGUF Q4_K: scale = d*sc, bias = 8*scale - dmin*m); mb_moe_prefill only */
+                          (GGUF Q4_K: scale = d*sc, bias = 8*scale - dmin*m) */
 };
 
 const char *mb_last_error(void);
@@ -149,7 +149,10 @@ int64_t mb_moe_decode_workspace_bytes(int64_t P, int I);
  * max_rows, its picks offsets[e]..offsets[e+1] of the sorted order (rows of
  * x given by sorted_rows) are run through gate|up, SiLU(gate) * up and down:
  * y (P, H) f32 gets the unweighted expert output of each pick.  Pass row_exp
- * from mb_router_logits / mb_row_exponents.  fmt_gu / fmt_down: MB_FMT_*.
+ * from mb_router_logits / mb_row_exponents.  fmt_gu / fmt_down: MB_FMT_*
+ * (GGUF Q4_K gate|up as MB_FMT_Q4K_F32: moelan/kernels.py:499-527 _mv_q4_k).
+ * Any H and I (multiples of gs and of 4); K above 2048 is taken in windows of
+ * 2048 columns.
  * status: a device word the kernels OR MB_STATUS bits into, or NULL to use
  * a word inside the workspace. */
 int mb_moe_decode(const MbExpert *table, int E, int H, int I, int gs, int fmt_gu, int fmt_down, const float *x,

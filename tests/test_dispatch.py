@@ -2,8 +2,8 @@
 entry points replaced by recorders: the decode mat-vecs for small batches,
 both kernels for mid-sized ones (experts below gemm_min_rows picks on the
 decode kernel), every expert on the grouped GEMM once the picks average twice
-gemm_min_rows, and always the grouped GEMM for experts the decode kernel
-cannot take (affine int4, K > 2048)."""
+gemm_min_rows, for every weight format and size (affine int4, K > 2048
+included)."""
 
 import sys
 import types
@@ -44,9 +44,11 @@ def test_kernel_choice_by_batch(monkeypatch, T, want):
     assert _run(monkeypatch, _experts(), T * 8) == want
 
 
-def test_affine_and_wide_experts_always_use_the_gemm(monkeypatch):
-    assert _run(monkeypatch, _experts(fmt=L.FMT_Q4K_F32), 1) == [("gemm", 1)]
-    assert _run(monkeypatch, _experts(E=8, H=4096, I=14336, fmt=L.FMT_Q8_F16), 2) == [("gemm", 1)]
+def test_affine_and_wide_experts_follow_the_batch(monkeypatch):
+    # GGUF Q4_K (affine int4) and K > 2048 run on the decode kernels at decode sizes too
+    assert _run(monkeypatch, _experts(fmt=L.FMT_Q4K_F32), 1) == [("decode", 0)]
+    assert _run(monkeypatch, _experts(E=8, H=4096, I=14336, fmt=L.FMT_Q8_F16), 2) == [("decode", 0)]
+    assert _run(monkeypatch, _experts(E=8, H=4096, I=14336, fmt=L.FMT_Q4K_F32), 1024) == [("gemm", 1)]
 
 
 def test_expert_parallel_slice_decides_by_its_own_picks(monkeypatch):
@@ -57,15 +59,15 @@ def test_expert_parallel_slice_decides_by_its_own_picks(monkeypatch):
     assert _run(monkeypatch, ex, 16384, picks=2048) == [("gemm", 1)]
 
 
-def test_gemm_only_experts_without_exponents_raise(monkeypatch):
-    # experts stored from raw tiles without the tensor-core exponents cannot run as grouped GEMMs
+def test_experts_without_exponents_stay_on_the_decode_kernels(monkeypatch):
+    # experts stored from raw tiles without the tensor-core exponents never reach the grouped GEMM
     ex = _experts(fmt=L.FMT_Q4K_F32)
     ex.missing_exp = {3}
-    with pytest.raises(ValueError, match="exponents"):
-        _run(monkeypatch, ex, 1)
+    assert _run(monkeypatch, ex, 1) == [("decode", 0)]
+    assert _run(monkeypatch, ex, 65536) == [("decode", 0)]
 
 
 def test_largest_permutation_reaches_the_gemm(monkeypatch):
-    # mb_permute takes up to 65536 picks and so does the grouped GEMM: T=8192, k=8 on a GEMM-only layer
+    # mb_permute takes up to 65536 picks (T=8192, k=8) and so does the grouped GEMM
     assert _run(monkeypatch, _experts(fmt=L.FMT_Q4K_F32), 65536) == [("gemm", 1)]
     assert _run(monkeypatch, _experts(), 65536) == [("gemm", 1)]

@@ -234,6 +234,55 @@ def test_gguf_q8_0_and_q4_0_matmul(D, golden, rows):
     assert row_err(got, golden[f"gguf_mm_2_{rows}"]) < TOL_F32
 
 
+@pytest.mark.parametrize("K", [2176, 4096, 14336])
+@pytest.mark.parametrize("n", [1, 6])
+def test_matmul_wide_k_windows(D, K, n):
+    """K above 2048 runs in windows of 2048 columns: int4 (f16 scales),
+    int8 (f32 scales) and the affine int4 form of GGUF Q4_K."""
+    from distributedmoellm_b200 import layout as L
+    rng = np.random.default_rng(K + n)
+    O_ = 72
+    x = rng.standard_normal((n, K)).astype(np.float32)
+    raw = rng.integers(0, 256, (O_, K // 2), dtype=np.uint8)
+    s = (rng.random((O_, K // 32), dtype=np.float32) * 1e-2).astype(np.float16)
+    got = D.matmul_t(cu(L.q4_tiles(raw, s, 32, False)), L.FMT_Q4_F16, O_, K, cu(x)).cpu().numpy()
+    assert row_err(got, O.q4_matmul_t(x, raw, s.astype(np.float32), 32, False)) < TOL_F32
+    q = rng.integers(-127, 128, (O_, K), dtype=np.int8)
+    s8 = rng.random((O_, K // 64), dtype=np.float32) * 1e-3
+    got = D.matmul_t(cu(L.q8_tiles(q, s8, 64)), L.FMT_Q8_F32, O_, K, cu(x)).cpu().numpy()
+    assert row_err(got, O.q8_matmul_t(x, q, s8, 64)) < TOL_F32
+    if K % 256 == 0:
+        g = C.gguf_random_rows(O_, K, 12, rng, 0.01)
+        got = D.matmul_t(cu(L.q4k_tiles(g, K)), L.FMT_Q4K_F32, O_, K, cu(x)).cpu().numpy()
+        w = O.gguf_dequant(g, 12, K).astype(np.float64)
+        assert row_err(got, x.astype(np.float64) @ w.T) < TOL_F32
+
+
+@pytest.mark.parametrize("T", [1, 5, 40])
+def test_wide_layer_decode_matches_oracle(D, T):
+    """A layer whose gate|up (K = H = 3072) and down (K = I = 2560) both run in
+    two K windows, the second one narrow (8 and 4 of 16 quads), through the
+    decode kernels only: 1, 5 and 40 tokens (chunks of up to 8 picks, several
+    segments per chunk)."""
+    from distributedmoellm_b200 import synthetic as S
+    rng = np.random.default_rng(90 + T)
+    cfg = dict(H=3072, I=2560, E=8, k=2, gs=32)
+    experts = {e: C.int4_expert(rng, cfg["H"], cfg["I"], 32, f16_scales=True) for e in range(cfg["E"])}
+    router = rng.standard_normal((cfg["E"], cfg["H"])).astype(np.float32)
+    layer = _layer(cfg, "q4", experts, router, f16=True)
+    layer.gemm_min_rows = 0
+    x = S.hidden(rng, T, cfg["H"])
+    out = layer(cu(x)).cpu().numpy()
+    b = layer.buffers(T)
+    idx, w = b.idx.cpu().numpy(), b.w.cpu().numpy()
+    e_, off, rows, wts = O.group_by_expert(idx, w)
+    groups = [(e_[i], rows[off[i]:off[i + 1]], wts[off[i]:off[i + 1]]) for i in range(len(e_))]
+    desc = {e: (("q4", g, gs_, 32, False), ("q4", d, ds, 32, False)) for e, (g, gs_, d, ds) in experts.items()}
+    want = O.store_compute(x, groups, desc, cfg["I"])
+    assert row_err(out, want) < TOL_F32
+    assert layer.status(T) == 0
+
+
 @pytest.mark.parametrize("qt", sorted(C.GGUF_BLOCK))
 @pytest.mark.parametrize("rows", C.GGUF_MM_ROWS)
 def test_gguf_matmul_all_types(D, golden, qt, rows):
