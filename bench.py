@@ -221,16 +221,64 @@ class Clocks:
 
 # ---- CPU side: the reference's algorithm (oracle restatement) -----------------------------
 
+REF = ROOT / "baseline" / "_ref"
+
+
+class _Threads:
+    """Thread control of one CPU implementation: ``set(n)`` / ``get()``."""
+
+    def __init__(self, set_fn, get_fn):
+        self.set, self.get = set_fn, get_fn
+
+
 def cpu_step_fn(experts, router, T, seed=7):
+    """One MoE-layer step of the reference's CPU algorithm on the same inputs:
+    moelan itself when it is installed under baseline/_ref (model.route,
+    group_by_expert and ExpertStore.compute over in-memory Packed4 experts,
+    numba kernels with exact f32 activations, MOELAN_INT8_ACT=0), else the C
+    restatement in oracle/.  Returns (step, threads control, kind, what)."""
+    x = np.random.default_rng(seed).standard_normal((T, H), dtype=np.float32)
+    if (REF / "moelan").is_dir():
+        import tempfile
+        os.environ["MOELAN_INT8_ACT"] = "0"
+        os.environ.setdefault("NUMBA_CACHE_DIR", tempfile.mkdtemp(prefix="numba_"))
+        sys.path.insert(0, str(REF))
+        import numba
+        from moelan import model as M
+        from moelan.experts import Expert, ExpertStore, Packed4
+
+        class MemSource:
+            zero_copy = False
+
+            def __init__(self, ex):
+                self.ex = ex
+
+            def has(self, key):
+                return key[1] in self.ex
+
+            def load(self, key):
+                return self.ex[key[1]]
+
+        objs = {e: Expert(Packed4(gr, np.ascontiguousarray(gsc, np.float32), GS, (2 * I, H)),
+                          Packed4(dr, np.ascontiguousarray(dsc, np.float32), GS, (H, I)), I)
+                for e, (gr, gsc, dr, dsc) in experts.items()}
+        store = ExpertStore([MemSource(objs)], fmt="int4")
+
+        def step():
+            idx, w = M.route(x @ router.T, K_TOP, True)
+            ex, off, rows, wts = M.group_by_expert(idx, w)
+            groups = [(ex[i], rows[off[i]:off[i + 1]], wts[off[i]:off[i + 1]]) for i in range(len(ex))]
+            return store.compute(0, x, groups)
+        thr = _Threads(numba.set_num_threads, numba.get_num_threads)
+        return step, thr, "reference", "moelan (baseline/_ref): route + group_by_expert + ExpertStore.compute, numba"
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle as O
     desc = {e: (("q4", gr, gsc.astype(np.float32), GS, False), ("q4", dr, dsc.astype(np.float32), GS, False))
             for e, (gr, gsc, dr, dsc) in experts.items()}
-    x = np.random.default_rng(seed).standard_normal((T, H), dtype=np.float32)
 
     def step():
         return O.moe_layer(x, router, desc, K_TOP, True, I)[0]
-    return step, O
+    return step, _Threads(O.set_threads, O.threads), "port", "C+OpenMP restatement of moelan's fused int4 layer"
 
 
 def host_threads() -> int:
@@ -242,19 +290,20 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
-def time_cpu(step, O, warmup=1, max_steps=200, budget_s=12.0):
+def time_cpu(step, thr, warmup=1, max_steps=200, budget_s=12.0):
     """The one CPU timing of the reference's algorithm, used by both the GPU
-    arm's cpu_baseline and the reference arm: the oracle's OpenMP threads set
-    to every host core, ``warmup`` untimed steps, then up to ``max_steps``
-    steps or ``budget_s`` seconds.  Returns (seconds per step, steps, threads)."""
-    O.set_threads(host_threads())
+    arm's cpu_baseline and the reference arm: its threads set to every host
+    core, ``warmup`` untimed steps (numba compiles on the first), then up to
+    ``max_steps`` steps or ``budget_s`` seconds.  Returns (seconds per step,
+    steps, threads)."""
+    thr.set(host_threads())
     for _ in range(max(1, warmup)):
         step()  # warm (thread pools, page-in)
     n, t0 = 0, time.perf_counter()
     while n < max_steps and (n == 0 or time.perf_counter() - t0 < budget_s):
         step()
         n += 1
-    return (time.perf_counter() - t0) / n, n, O.threads()
+    return (time.perf_counter() - t0) / n, n, thr.get()
 
 
 # ---- GPU side ---------------------------------------------------------------------------------
@@ -580,11 +629,10 @@ def run_gpu(args, rank, world, dev):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        step, O = cpu_step_fn(experts, router, T)
-        s_per, n, thr = time_cpu(step, O)
-        cpu = {"value": round(T / s_per, 2), "unit": UNIT, "cores": thr, "kind": "port",
-               "sample": f"{n} MoE-layer steps of T={T} tokens (all 128 experts resident in host RAM), "
-                         f"C+OpenMP restatement of moelan's fused int4 layer kernel + numpy routing"}
+        step, tc, kind, what = cpu_step_fn(experts, router, T)
+        s_per, n, thr = time_cpu(step, tc, warmup=2)
+        cpu = {"value": round(T / s_per, 2), "unit": UNIT, "cores": thr, "kind": kind,
+               "sample": f"{n} MoE-layer steps of T={T} tokens (all 128 experts resident in host RAM), {what}"}
     return value, ms, roof, e2e, sweep, cpu, clk.summary(), status, prefill, e2e_dropin
 
 
@@ -669,16 +717,16 @@ def measure_e2e(layers, T, steps, warmup, world, dev):
 def run_reference(args):
     """The reference arm: moelan's CPU algorithm (oracle restatement) on all host cores."""
     experts, router = make_experts(0)
-    step, O = cpu_step_fn(experts, router, args.tokens)
-    s_per, n, thr = time_cpu(step, O, warmup=args.warmup, max_steps=args.steps, budget_s=120.0)
+    step, tc, kind, what = cpu_step_fn(experts, router, args.tokens)
+    s_per, n, thr = time_cpu(step, tc, warmup=max(2, args.warmup), max_steps=args.steps, budget_s=120.0)
     ms = 1e3 * s_per
     value = args.tokens / (ms / 1e3)
     return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "impl": "reference",
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": workload_config(args),
-            "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": thr, "kind": "port",
-                             "sample": f"{n} MoE-layer steps of T={args.tokens}"},
+            "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": thr, "kind": kind,
+                             "sample": f"{n} MoE-layer steps of T={args.tokens}, {what}"},
             "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
