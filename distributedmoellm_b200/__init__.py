@@ -23,11 +23,11 @@ __version__ = "0.1.0"
 
 def install(moelan_module=None):
     """Patch moelan's expert-compute entry points with the B200 path."""
-    from .install import install as _install
+    from .dropin import install as _install
     return _install(moelan_module)
 
 
 def uninstall(saved):
     """Undo :func:`install` (``saved``: what it returned)."""
-    from .install import uninstall as _uninstall
+    from .dropin import uninstall as _uninstall
     return _uninstall(saved)

@@ -48,10 +48,28 @@ namespace {
 
 constexpr int kMaxKW = 16;      // MMA warps: one per quad (128 columns) of a K window of up to 2048 columns
 constexpr int kEpiWarps = 2;    // epilogue warps, taking alternate items (one warp with K windows)
-constexpr int kMaxMT = 4;       // row tiles per stage
+#ifndef MB_DECODE_MAX_MT
+#define MB_DECODE_MAX_MT 6
+#endif
+constexpr int kMaxMT = MB_DECODE_MAX_MT;   // row tiles per stage
 constexpr int kRedTile = 128;   // floats of one warp's partial of one tile: [8 input rows][16 rows]
 constexpr int kMaxCachedE = 1024;  // experts whose weight address the kernel keeps in shared memory
 constexpr int kMaxCachedP = 1024;  // picks whose token row and exponent the kernel keeps in shared memory
+#ifndef MB_DECODE_WAIT
+#define MB_DECODE_WAIT mb_mbar_wait   // the MMA and epilogue warps' waits (mb_mbar_wait_spin: no sleeps)
+#endif
+#ifndef MB_DECODE_STAGE_KB
+#define MB_DECODE_STAGE_KB 48   // target bytes of one stage of row tiles, in KB
+#endif
+#ifndef MB_DECODE_STAGE_KB_SMALL
+#define MB_DECODE_STAGE_KB_SMALL 32   // the same for calls of at most MB_DECODE_SMALL_P picks
+#endif
+#ifndef MB_DECODE_SMALL_P
+#define MB_DECODE_SMALL_P 16
+#endif
+#ifndef MB_DECODE_NRED
+#define MB_DECODE_NRED 2        // reduction slots per epilogue warp with many MMA warps
+#endif
 constexpr int kSegTiles = 32;   // K > 2048: row tiles of a segment whose partial sums wait in shared memory
 
 struct Fmt {
@@ -256,6 +274,12 @@ struct WinCursor {
         rem = hi - lo;
         j = w = 0;
         seg_init(RTS, SEG);
+    }
+    // With one window the items are the units: only the unit cursor moves.
+    __device__ __forceinline__ void advance(const int64_t* pre, int E, int RTS, int SEG, int NW)
+    {
+        if (NW == 1) u.next(pre, E, RTS);
+        else next(pre, E, RTS, SEG, NW);
     }
     __device__ __forceinline__ void next(const int64_t* pre, int E, int RTS, int SEG, int NW)
     {
@@ -487,7 +511,7 @@ __global__ void __launch_bounds__(kThreadsMax, 1) moe_decode_kernel(const __grid
             uint32_t ph = 0;
             int we = -1;
             const uint8_t* wbase = nullptr;
-            for (int64_t it = 0; it < n_items; ++it, cur.next(pre, E, RTS, SEG, NW)) {
+            for (int64_t it = 0; it < n_items; ++it, cur.advance(pre, E, RTS, SEG, NW)) {
                 if (it >= S && !mb_mbar_wait(&empty[s], ph ^ 1u, a.status, abort_flag)) break;
                 if (cur.u.e != we) {
                     we = cur.u.e;
@@ -541,7 +565,7 @@ __global__ void __launch_bounds__(kThreadsMax, 1) moe_decode_kernel(const __grid
             if (rg == 0 && n < nvalid) atomicMax(&a.act_max[pbase + n], __float_as_uint(m));
             rmax = 0.f;
         };
-        for (int64_t it = 0; it < n_items; ++it, cur.next(pre, E, RTS, SEG, NW)) {
+        for (int64_t it = 0; it < n_items; ++it, cur.advance(pre, E, RTS, SEG, NW)) {
             const int r = rnext;
             const uint32_t rph = rphn;
             if (++rnext == NR) {
@@ -563,7 +587,7 @@ __global__ void __launch_bounds__(kThreadsMax, 1) moe_decode_kernel(const __grid
                 }
                 fs = pow2f(-ex);
             }
-            const bool ok = mb_mbar_wait(&rfull[r], rph, a.status, abort_flag);
+            const bool ok = MB_DECODE_WAIT(&rfull[r], rph, a.status, abort_flag);
             const int nt = min(MT, RT - cur.u.sg * MT);
             if (ok) {
                 const float* rr = red + r * red_buf;
@@ -641,7 +665,7 @@ __global__ void __launch_bounds__(kThreadsMax, 1) moe_decode_kernel(const __grid
     bool two = false, has = false;
     int s = 0, r = 0;
     uint32_t ph = 0, rph = 0;
-    for (int64_t it = 0; it < n_items; ++it, cur.next(pre, E, RTS, SEG, NW)) {
+    for (int64_t it = 0; it < n_items; ++it, cur.advance(pre, E, RTS, SEG, NW)) {
         if (cur.u.e != ke || cur.u.c != kc || cur.w != kw) {
             ke = cur.u.e;
             kc = cur.u.c;
@@ -710,8 +734,8 @@ __global__ void __launch_bounds__(kThreadsMax, 1) moe_decode_kernel(const __grid
         }
 
         const int ntiles = min(MT, RT - cur.u.sg * MT);
-        if (it >= NR) mb_mbar_wait(&rempty[r], rph ^ 1u, a.status, abort_flag);
-        const bool ok = mb_mbar_wait(&full[s], ph, a.status, abort_flag);
+        if (it >= NR) MB_DECODE_WAIT(&rempty[r], rph ^ 1u, a.status, abort_flag);
+        const bool ok = MB_DECODE_WAIT(&full[s], ph, a.status, abort_flag);
         float* rb = red + r * red_buf + warp * MT * kRedTile;
         if (ok) {
             const uint8_t* stage = stages + (size_t)s * stage_bytes + warp * kBlock;
@@ -762,31 +786,38 @@ Cfg plan(int fmt, int K, int E, int RT, int P, int phase)
     c.NW = (c.NQ + c.QW - 1) / c.QW;
     c.tile_bytes = c.NQ * f.block_bytes;
     const int wt = c.QW * f.block_bytes;
-    c.MT = (32 * 1024 + wt / 2) / wt;
-    c.MT = c.MT < 1 ? 1 : (c.MT > kMaxMT ? kMaxMT : c.MT);
-    if (c.MT > RT) c.MT = RT < 1 ? 1 : RT;
-    c.SEG = c.NW > 1 ? (kSegTiles / c.MT > 0 ? kSegTiles / c.MT : 1) : (1 << 30);
+    // stages of ~48 KB (fewer hand-offs per byte), ~32 KB for a handful of picks, where more and
+    // smaller units spread the little work there is over more SMs
+    const int stage_kb = P <= MB_DECODE_SMALL_P ? MB_DECODE_STAGE_KB_SMALL : MB_DECODE_STAGE_KB;
+    int mt0 = (stage_kb * 1024 + wt / 2) / wt;
+    mt0 = mt0 < 1 ? 1 : (mt0 > kMaxMT ? kMaxMT : mt0);
+    if (mt0 > RT) mt0 = RT < 1 ? 1 : RT;
     // reduction buffers: with many MMA warps each epilogue warp keeps two items in
     // hand (the MMA warps run further ahead); with few, shared memory goes to stages
-    c.nred = c.KW > 8 ? 2 * kEpiWarps : kEpiWarps;
+    c.nred = c.KW > 8 ? MB_DECODE_NRED * kEpiWarps : kEpiWarps;
     // one CTA per SM with many MMA warps, two with few (113 KB each leaves the per-CTA reserve)
     const size_t budget = c.KW <= 8 ? 113 * 1024 : 220 * 1024;
-    const size_t red = (size_t)c.nred * c.KW * c.MT * kRedTile * sizeof(float);
-    const size_t seg = c.NW > 1 ? (size_t)c.SEG * c.MT * kRedTile * sizeof(float) : 0;
     const size_t cache = 2 * (size_t)(E + 1) * sizeof(int64_t) + (E <= kMaxCachedE ? (size_t)E * sizeof(void*) : 0) +
                          2 * (size_t)E * sizeof(int32_t);
-    const size_t stage = (size_t)c.MT * wt;
-    auto stages_for = [&](size_t fixed) {
-        const int st = budget > fixed ? (int)((budget - fixed) / stage) : 2;
-        return st < 2 ? 2 : (st > 8 ? 8 : st);
-    };
-    const size_t fixed = red + seg + cache + 64 + 16 * sizeof(uint64_t);
-    // the picks' rows and exponents go to shared memory only where that costs no weight stage
-    const size_t pcache = P <= kMaxCachedP ? (phase == 1 ? 2 : 1) * (size_t)P * sizeof(int32_t) : 0;
-    c.stages = stages_for(fixed);
-    c.pc = (pcache && stages_for(fixed + pcache) == c.stages) ? P : 0;
-    c.smem = (size_t)c.stages * stage + red + seg + (size_t)(2 * c.stages + 2 * c.nred) * sizeof(uint64_t) + cache +
-             (c.pc ? pcache : 0) + 16;
+    // the largest stage that leaves room for at least two of them
+    for (c.MT = mt0;; --c.MT) {
+        c.SEG = c.NW > 1 ? (kSegTiles / c.MT > 0 ? kSegTiles / c.MT : 1) : (1 << 30);
+        const size_t red = (size_t)c.nred * c.KW * c.MT * kRedTile * sizeof(float);
+        const size_t seg = c.NW > 1 ? (size_t)c.SEG * c.MT * kRedTile * sizeof(float) : 0;
+        const size_t stage = (size_t)c.MT * wt;
+        auto stages_for = [&](size_t fixed) {
+            const int st = budget > fixed ? (int)((budget - fixed) / stage) : 2;
+            return st < 2 ? 2 : (st > 8 ? 8 : st);
+        };
+        const size_t fixed = red + seg + cache + 64 + 16 * sizeof(uint64_t);
+        // the picks' rows and exponents go to shared memory only where that costs no weight stage
+        const size_t pcache = P <= kMaxCachedP ? (phase == 1 ? 2 : 1) * (size_t)P * sizeof(int32_t) : 0;
+        c.stages = stages_for(fixed);
+        c.pc = (pcache && stages_for(fixed + pcache) == c.stages) ? P : 0;
+        c.smem = (size_t)c.stages * stage + red + seg + (size_t)(2 * c.stages + 2 * c.nred) * sizeof(uint64_t) +
+                 cache + (c.pc ? pcache : 0) + 16;
+        if (c.smem <= budget + 7 * 1024 || c.MT == 1) break;
+    }
     return c;
 }
 
@@ -795,6 +826,8 @@ int launch_phase(const DecodeArgs& base, int K, int RT, cudaStream_t st)
 {
     DecodeArgs a = base;
     const Cfg c = plan(FMT, K, a.E, RT, a.P, a.phase);
+    if (c.smem > 227 * 1024)
+        return mb_fail(MB_EUNSUPPORTED, "mb_moe_decode: %d experts leave no room for two weight stages", a.E);
     a.K = K;
     a.NQ = c.NQ;
     a.QW = c.QW;

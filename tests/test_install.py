@@ -84,7 +84,7 @@ def test_pack_gguf_q4_k_reproduces_the_reference_weights():
 def _fake_moelan():
     k = types.ModuleType("fake_moelan.kernels")
     a = types.ModuleType("fake_moelan.accel")
-    from distributedmoellm_b200.install import ACCEL_NAMES, KERNEL_NAMES
+    from distributedmoellm_b200.dropin import ACCEL_NAMES, KERNEL_NAMES
     for n in KERNEL_NAMES:
         setattr(k, n, ("orig", n))
     for n in ACCEL_NAMES:
@@ -98,7 +98,7 @@ def test_install_refuses_without_a_device():
     import torch
     if torch.cuda.is_available():
         pytest.skip("a CUDA device is present")
-    from distributedmoellm_b200.install import install
+    from distributedmoellm_b200.dropin import install
     pkg = _fake_moelan()
     with pytest.raises(RuntimeError):
         install(pkg)
@@ -107,7 +107,7 @@ def test_install_refuses_without_a_device():
 
 def test_install_patches_and_uninstall_restores(monkeypatch):
     from distributedmoellm_b200 import accel, device, kernels
-    from distributedmoellm_b200.install import ACCEL_NAMES, KERNEL_NAMES, install, uninstall
+    from distributedmoellm_b200.dropin import ACCEL_NAMES, KERNEL_NAMES, install, uninstall
     monkeypatch.setattr(device, "require_device", lambda: None)
     pkg = _fake_moelan()
     saved = install(pkg)
@@ -134,7 +134,7 @@ def test_install_covers_the_reference_entry_points(monkeypatch):
     mk = pytest.importorskip("moelan.kernels")
     ma = pytest.importorskip("moelan.accel")
     from distributedmoellm_b200 import accel, kernels
-    from distributedmoellm_b200.install import ACCEL_NAMES, KERNEL_NAMES
+    from distributedmoellm_b200.dropin import ACCEL_NAMES, KERNEL_NAMES
     for mod, ours, names in ((mk, kernels, KERNEL_NAMES), (ma, accel, ACCEL_NAMES)):
         for n in names:
             ref = getattr(mod, n)
@@ -145,3 +145,17 @@ def test_install_covers_the_reference_entry_points(monkeypatch):
     for m in ("expert_bytes", "add", "launch", "launch_held", "release", "collect", "calibrate", "stats"):
         assert list(inspect.signature(getattr(ma.GpuTier, m)).parameters) == \
             list(inspect.signature(getattr(accel.GpuTier, m)).parameters), m
+
+
+def test_package_install_stays_callable(monkeypatch):
+    """distributedmoellm_b200.install is the function on every call: the
+    patching code lives in a submodule of another name, so importing it does
+    not rebind the package attribute."""
+    import distributedmoellm_b200 as mb
+    from distributedmoellm_b200 import device
+    monkeypatch.setattr(device, "require_device", lambda: None)
+    for _ in range(2):
+        pkg = _fake_moelan()
+        saved = mb.install(pkg)
+        assert callable(mb.install) and callable(mb.uninstall)
+        mb.uninstall(saved)
