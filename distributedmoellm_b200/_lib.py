@@ -23,6 +23,9 @@ SIGNATURES = {
     "mb_q8_dequant": (_int, [_vp, _vp, _int, _i64, _i64, _int, _vp, _vp]),
     "mb_gguf_dequant": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _vp]),
     "mb_gguf_matmul_t": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),
+    "mb_wire_group": (_int, [_int]),
+    "mb_encode_rows": (_int, [_vp, _i64, _int, _int, _vp, _vp, _vp]),
+    "mb_decode_rows": (_int, [_vp, _vp, _i64, _int, _int, _vp, _vp]),
     "mb_router_workspace_bytes": (_i64, [_i64, _int, _int]),
     "mb_router_logits": (_int, [_vp, _vp, _i64, _int, _int, _vp, _vp, _vp, _i64, _vp]),
     "mb_router_route": (_int, [_vp, _vp, _i64, _int, _int, _int, _int, _vp, _vp, _vp, _vp, _vp, _i64, _vp]),

@@ -78,6 +78,40 @@ def gguf_matmul_t(raw: torch.Tensor, qtype: int, cols: int, x: torch.Tensor, y: 
     return y
 
 
+# ---- activation rows in the wire formats (moelan/protocol.py:96-123) -------------------
+
+WIRE = {"f16": 1, "int8": 2}
+
+
+def encode_rows(a: torch.Tensor, wire: str):
+    """(q, scales) of f32 rows a (n, d) in wire format "f16" or "int8"
+    (scales None for f16); "f32" returns a itself."""
+    _cuda(a)
+    if wire == "f32":
+        return a, None
+    n, d = a.shape
+    if wire == "f16":
+        q = torch.empty((n, d), dtype=torch.float16, device=a.device)
+        sc = None
+    else:
+        q = torch.empty((n, d), dtype=torch.int8, device=a.device)
+        sc = torch.empty((n, d // int(lib().mb_wire_group(d))), dtype=torch.float32, device=a.device)
+    check(lib().mb_encode_rows(_p(a), n, d, WIRE[wire], _p(q), _p(sc), _stream()), "mb_encode_rows")
+    return q, sc
+
+
+def decode_rows(q: torch.Tensor, scales: torch.Tensor | None = None, out: torch.Tensor | None = None):
+    """f32 rows from f16 rows, or from int8 rows and their scales."""
+    _cuda(q, scales, out)
+    if q.dtype == torch.float32:
+        return q
+    n, d = q.shape
+    wire = WIRE["f16"] if q.dtype == torch.float16 else WIRE["int8"]
+    out = torch.empty((n, d), dtype=torch.float32, device=q.device) if out is None else out
+    check(lib().mb_decode_rows(_p(q), _p(scales), n, d, wire, _p(out), _stream()), "mb_decode_rows")
+    return out
+
+
 # ---- router -------------------------------------------------------------------------
 
 def router_workspace_bytes(T: int, H: int, E: int) -> int:

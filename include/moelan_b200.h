@@ -47,6 +47,12 @@ enum {
                           (GGUF Q4_K: scale = d*sc, bias = 8*scale - dmin*m) */
 };
 
+/* Wire formats of activation rows (moelan/protocol.py:96 WIRE_FORMATS; f32 rows need no conversion). */
+enum {
+    MB_WIRE_F16 = 1, /* f16, round to nearest even */
+    MB_WIRE_INT8 = 2 /* int8, one f32 scale per group of mb_wire_group(d) values */
+};
+
 const char *mb_last_error(void);
 int mb_version(void);
 /* MB_OK when the current device is an sm_100 part this build runs on. */
@@ -81,6 +87,22 @@ int mb_gguf_dequant(const uint8_t *raw, int qtype, int64_t rows, int64_t row_byt
  * y (n, rows) f32, x 16-byte aligned. */
 int mb_gguf_matmul_t(const uint8_t *raw, int qtype, int64_t rows, int64_t row_bytes, int64_t cols, const float *x,
                      int64_t n, float *y, void *stream);
+
+/* ---- activation rows in the wire formats --------------------------------------- */
+
+/* Values per int8 scale for rows of width d: 64 when d is a multiple of 64,
+ * else the whole row (moelan/protocol.py:96-97, 108). */
+int mb_wire_group(int d);
+
+/* moelan/protocol.py:99-114 encode_rows(a, wire, name) on the device, bit-exact:
+ * a (n, d) f32 -> q (n, d) f16 (MB_WIRE_F16) or int8 (MB_WIRE_INT8) with scales
+ * (n, d / mb_wire_group(d)) f32 = max|group| / 127 (1 for an all-zero group) and
+ * q = clip(rint(a / scale), -127, 127). */
+int mb_encode_rows(const float *a, int64_t n, int d, int wire, void *q, float *scales, void *stream);
+
+/* moelan/protocol.py:117-123 decode_rows(arrays, name) on the device, bit-exact:
+ * q (n, d) f16 or int8 (with its scales) -> out (n, d) f32. */
+int mb_decode_rows(const void *q, const float *scales, int64_t n, int d, int wire, float *out, void *stream);
 
 /* ---- router ------------------------------------------------------------------ */
 

@@ -170,3 +170,20 @@ def layer_inputs(cfg, kind="int4", f16_scales=False):
                           gguf_random_rows(H, I, 8, rng, 0.001))
     x = rng.standard_normal((cfg["T"], H)).astype(np.float32)
     return x, router, experts
+
+
+# ---- activation rows in the wire formats (moelan/protocol.py:96-123) ---------------
+
+def wire_inputs():
+    """Rows for encode_rows / decode_rows: the reference test's own case
+    (tests/test_moelan.py:998-1009: N(0, 3) rows with one outlier channel x40),
+    a width that is not a multiple of 64 (one scale per row), all-zero rows,
+    and a row whose quotients fall exactly halfway (rint rounds half to even)."""
+    rng = np.random.default_rng(6)
+    a = rng.standard_normal((5, 2048)).astype(np.float32) * 3
+    a[:, 7] *= 40
+    b = rng.standard_normal((7, 96)).astype(np.float32)
+    z = np.zeros((2, 8), np.float32)
+    h = np.zeros((1, 64), np.float32)
+    h[0, :8] = [127.0, 2.5, 3.5, -0.5, -1.5, 126.5, -126.5, 0.5]
+    return {"wide": a, "narrow": b, "zeros": z, "halfway": h}

@@ -138,6 +138,16 @@ def main(ref_root: str) -> None:
     kernels.moe_q4(x[:2], items, C.LAYER_F16["H"], C.LAYER_F16["I"], 32, out)
     g["moe_q4_mixed_out"] = out
 
+    # activation rows in the wire formats (moelan/protocol.py:99-123)
+    from moelan.protocol import decode_rows, encode_rows
+    for name, a in C.wire_inputs().items():
+        for wire in ("f16", "int8"):
+            enc = encode_rows(a, wire, "x")
+            g[f"wire_{name}_{wire}_q"] = enc["x"]
+            if wire == "int8":
+                g[f"wire_{name}_{wire}_s"] = enc["x_scale"]
+            g[f"wire_{name}_{wire}_dec"] = decode_rows(enc, "x")
+
     np.savez_compressed(HERE / "golden.npz", **g)
     print("wrote", HERE / "golden.npz", sum(v.nbytes for v in g.values()), "bytes (uncompressed)")
 

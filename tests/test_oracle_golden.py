@@ -127,3 +127,18 @@ def test_moe_q4_mixed_raw_and_resident(golden):
     out = np.zeros((2, C.LAYER_F16["H"]), np.float32)
     O.moe_q4(x[:2], items, C.LAYER_F16["H"], C.LAYER_F16["I"], 32, out)
     _close_rows(out, golden["moe_q4_mixed_out"], 1e-5)
+
+
+@pytest.mark.parametrize("name", ["wide", "narrow", "zeros", "halfway"])
+@pytest.mark.parametrize("wire", ["f16", "int8"])
+def test_wire_rows_bit_exact(golden, name, wire):
+    """The wire-format restatement against the reference's encode_rows /
+    decode_rows (moelan/protocol.py:99-123): every byte and every decoded value."""
+    a = C.wire_inputs()[name]
+    q, s = O.encode_rows(a, wire)
+    assert q.dtype == golden[f"wire_{name}_{wire}_q"].dtype
+    assert np.array_equal(q.view(np.uint8), golden[f"wire_{name}_{wire}_q"].view(np.uint8))
+    if wire == "int8":
+        assert np.array_equal(s.view(np.uint32), golden[f"wire_{name}_{wire}_s"].view(np.uint32))
+    dec = O.decode_rows(q, s)
+    assert np.array_equal(dec.view(np.uint32), golden[f"wire_{name}_{wire}_dec"].view(np.uint32))
