@@ -30,6 +30,9 @@ SIGNATURES = {
     "mb_router_logits": (_int, [_vp, _vp, _i64, _int, _int, _vp, _vp, _vp, _i64, _vp]),
     "mb_router_route": (_int, [_vp, _vp, _i64, _int, _int, _int, _int, _vp, _vp, _vp, _vp, _vp, _i64, _vp]),
     "mb_router_topk": (_int, [_vp, _i64, _int, _int, _int, _vp, _vp, _vp]),
+    "mb_router_grouped": (_int, [_vp, _vp, _i64, _int, _int, _int, _int, _int, _int, _int, ctypes.c_float, _vp, _vp,
+                                 _vp]),
+    "mb_router_sparsemixer": (_int, [_vp, _i64, _int, ctypes.c_double, _vp, _vp, _vp]),
     "mb_row_exponents": (_int, [_vp, _i64, _int, _vp, _vp]),
     "mb_permute": (_int, [_vp, _vp, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "mb_unpermute_combine": (_int, [_vp, _vp, _vp, _vp, _i64, _int, _int, _int, _vp, _vp]),

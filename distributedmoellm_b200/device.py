@@ -167,6 +167,34 @@ def router_topk(logits: torch.Tensor, k: int, normalize: bool, idx=None, w=None)
     return idx, w
 
 
+GROUPED_METHODS = {"greedy": 0, "group_limited_greedy": 1, "noaux_tc": 2}
+
+
+def router_grouped(logits: torch.Tensor, k: int, scoring: str = "softmax", method: str = "greedy", n_group: int = 1,
+                   topk_group: int = 1, normalize: bool = True, scaling: float = 1.0, bias: torch.Tensor | None = None,
+                   idx=None, w=None):
+    """DeepSeek V2 / V3 routing (moelan/model.py:170-201); returns (idx, w)."""
+    _cuda(logits, bias)
+    T, E = logits.shape
+    idx = torch.empty((T, k), dtype=torch.int32, device=logits.device) if idx is None else idx
+    w = torch.empty((T, k), dtype=torch.float32, device=logits.device) if w is None else w
+    check(lib().mb_router_grouped(_p(logits), _p(bias), T, E, k, int(scoring == "sigmoid"), GROUPED_METHODS[method],
+                                  int(n_group), int(topk_group), int(bool(normalize)), float(scaling), _p(idx), _p(w),
+                                  _stream()), "mb_router_grouped")
+    return idx, w
+
+
+def router_sparsemixer(logits: torch.Tensor, eps: float, idx=None, w=None):
+    """PhiMoE's top-2 (moelan/model.py:204-223); returns (idx, w)."""
+    _cuda(logits)
+    T, E = logits.shape
+    idx = torch.empty((T, 2), dtype=torch.int32, device=logits.device) if idx is None else idx
+    w = torch.empty((T, 2), dtype=torch.float32, device=logits.device) if w is None else w
+    check(lib().mb_router_sparsemixer(_p(logits), T, E, float(eps), _p(idx), _p(w), _stream()),
+          "mb_router_sparsemixer")
+    return idx, w
+
+
 class Routing:
     """Device buffers of one permutation of T*k picks over E experts."""
 

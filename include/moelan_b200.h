@@ -127,6 +127,25 @@ int mb_router_route(const float *x, const float *router, int64_t T, int H, int E
 int mb_router_topk(const float *logits, int64_t T, int E, int k, int normalize, int32_t *idx, float *w,
                    void *stream);
 
+/* moelan/model.py:170-201 route_grouped(logits, cfg, bias): DeepSeek V2 / V3
+ * routing on f32 logits (T, E).  Scores: softmax (sigmoid = 0) or sigmoid (1)
+ * of the logits; choices: scores + bias (bias (E) f32, or NULL).  method 0
+ * greedy, 1 group_limited_greedy (groups ranked by their best choice), 2
+ * noaux_tc (by the sum of their two best); with method >= 1 and n_group > 1
+ * only the topk_group best of n_group equal groups keep their choices, the
+ * others' become 0.  idx (T, k): the k best choices (ties: lower id), w (T, k):
+ * their scores, divided by their sum + 1e-20 when k > 1 and normalize (and
+ * then multiplied by scaling for noaux_tc), else multiplied by scaling.
+ * E <= 1024, k <= 32, n_group <= 32. */
+int mb_router_grouped(const float *logits, const float *bias, int64_t T, int E, int k, int sigmoid, int method,
+                      int n_group, int topk_group, int normalize, float scaling, int32_t *idx, float *w, void *stream);
+
+/* moelan/model.py:204-223 route_sparsemixer(logits, eps): PhiMoE's top-2.
+ * Pick j is the best expert not yet picked, weighted by its softmax over the
+ * experts not yet picked whose logit l satisfies (best - l) / max(|l|, best)
+ * <= 2 * eps.  idx (T, 2) i32, w (T, 2) f32, not renormalised.  2 <= E <= 1024. */
+int mb_router_sparsemixer(const float *logits, int64_t T, int E, double eps, int32_t *idx, float *w, void *stream);
+
 /* Each row's power-of-two exponent (for inputs that did not come through
  * mb_router_logits). */
 int mb_row_exponents(const float *x, int64_t T, int H, int32_t *row_exp, void *stream);

@@ -187,3 +187,36 @@ def wire_inputs():
     h = np.zeros((1, 64), np.float32)
     h[0, :8] = [127.0, 2.5, 3.5, -0.5, -1.5, 126.5, -126.5, 0.5]
     return {"wide": a, "narrow": b, "zeros": z, "halfway": h}
+
+
+# ---- the other routers (moelan/model.py:170-223) -----------------------------------
+
+# (name, T, E, k, scoring, method, n_group, topk_group, normalize, scaling, with bias, seed)
+GROUPED_CASES = [
+    ("v3", 64, 256, 8, "sigmoid", "noaux_tc", 8, 4, True, 2.5, True, 41),
+    ("v3flat", 40, 64, 6, "sigmoid", "noaux_tc", 1, 1, True, 1.0, True, 42),
+    ("v2lim", 48, 64, 6, "softmax", "group_limited_greedy", 8, 3, False, 16.0, False, 43),
+    ("v2greedy", 33, 160, 6, "softmax", "greedy", 1, 1, False, 1.0, False, 44),
+    ("k1", 20, 32, 1, "sigmoid", "noaux_tc", 4, 2, True, 2.0, True, 45),
+]
+
+
+def grouped_inputs(T, E, with_bias, seed):
+    rng = np.random.default_rng(seed)
+    lg = rng.standard_normal((T, E)).astype(np.float32)
+    lg[1, 5] = lg[1, 9]                           # an exact tie between experts
+    lg[3, :] = 0.25                               # a row of equal logits
+    bias = (rng.standard_normal(E) * 0.05).astype(np.float32) if with_bias else None
+    return lg, bias
+
+
+def sparsemixer_inputs():
+    """The reference's own case (tests/test_hf_reference.py:59-72): near-ties
+    inside the 2 % band, negative maxima and exact zeros; plus a wider one."""
+    rng = np.random.default_rng(0)
+    base = rng.standard_normal((64, 16)).astype(np.float32)
+    base[::3, 1:4] = base[::3, :1] * np.float32(1 - 0.01 * rng.random((22, 3)))
+    base[1::4] = -np.abs(base[1::4])
+    base[2::5, :5] = 0.0
+    wide = np.random.default_rng(1).standard_normal((40, 48)).astype(np.float32)
+    return {"hf": base, "wide": wide}

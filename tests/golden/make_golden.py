@@ -148,6 +148,19 @@ def main(ref_root: str) -> None:
                 g[f"wire_{name}_{wire}_s"] = enc["x_scale"]
             g[f"wire_{name}_{wire}_dec"] = decode_rows(enc, "x")
 
+    # the other routers: DeepSeek grouped routing and PhiMoE's sparsemixer (moelan/model.py:170-223)
+    import types
+    for name, T, E, k, scoring, method, ng, tg, norm, scale, with_bias, seed in C.GROUPED_CASES:
+        lg, bias = C.grouped_inputs(T, E, with_bias, seed)
+        cfg = types.SimpleNamespace(scoring_func=scoring, topk_method=method, n_group=ng, topk_group=tg, top_k=k,
+                                    norm_topk_prob=norm, routed_scaling_factor=scale)
+        idx, w = model.route_grouped(lg, cfg, bias)
+        g[f"grouped_{name}_idx"], g[f"grouped_{name}_w"] = idx, w
+    for name, lg in C.sparsemixer_inputs().items():
+        for eps in (0.01, 0.1):
+            idx, w = model.route_sparsemixer(lg, eps)
+            g[f"sparse_{name}_{eps}_idx"], g[f"sparse_{name}_{eps}_w"] = idx, w
+
     np.savez_compressed(HERE / "golden.npz", **g)
     print("wrote", HERE / "golden.npz", sum(v.nbytes for v in g.values()), "bytes (uncompressed)")
 

@@ -455,3 +455,66 @@ def test_wire_rows_large_round_trip(D):
             dec = D.decode_rows(q, s).cpu().numpy()
             err = np.abs(dec - a)[:, 64:].max(1) / np.abs(a[:, 64:]).max(1)
             assert err.max() <= tol
+
+
+# ---- the other routers ----------------------------------------------------------------
+
+def _near_ties(v: np.ndarray, n: int, ulps: int = 4) -> np.ndarray:
+    """Rows whose n + 1 largest values hold two distinct ones within ulps f32
+    ulps: ranking them can differ through the last bit of an exponential."""
+    s = -np.sort(-v.astype(np.float32), axis=1)[:, :n + 1]
+    gap = s[:, :-1] - s[:, 1:]
+    return ((gap <= ulps * np.spacing(np.abs(s[:, :-1]))) & (gap != 0)).any(axis=1)
+
+
+@pytest.mark.parametrize("case", C.GROUPED_CASES, ids=[c[0] for c in C.GROUPED_CASES])
+def test_grouped_router_matches_reference(D, golden, case):
+    """mb_router_grouped against moelan's route_grouped: indices bit-exact
+    (rows with a near-tie among the deciding choices or group scores aside:
+    none in these cases is expected, and they are counted), weights within
+    2e-6 relative (the device's exp and sum order differ from numpy's in the
+    last bits)."""
+    name, T, E, k, scoring, method, ng, tg, norm, scale, with_bias, seed = case
+    lg, bias = C.grouped_inputs(T, E, with_bias, seed)
+    idx, w = D.router_grouped(cu(lg), k, scoring, method, ng, tg, norm, scale, None if bias is None else cu(bias))
+    idx, w = idx.cpu().numpy(), w.cpu().numpy()
+    _, _, choice = O.route_grouped(lg, k, scoring, method, ng, tg, norm, scale, bias)
+    skip = _near_ties(choice, k)
+    if method != "greedy" and ng > 1:
+        sc = 1.0 / (1.0 + np.exp(-lg)) if scoring == "sigmoid" else O.softmax(lg)
+        ch = (sc + bias[None, :]) if bias is not None else sc
+        g = ch.reshape(T, ng, E // ng)
+        gs = -np.sort(-g, axis=-1)[..., :2].sum(-1) if method == "noaux_tc" else g.max(-1)
+        skip |= _near_ties(gs, tg)
+    assert skip.sum() <= 2
+    want_i, want_w = golden[f"grouped_{name}_idx"], golden[f"grouped_{name}_w"]
+    assert np.array_equal(idx[~skip], want_i[~skip])
+    np.testing.assert_allclose(w[~skip], want_w[~skip], rtol=2e-6, atol=1e-12)
+
+
+@pytest.mark.parametrize("name", ["hf", "wide"])
+@pytest.mark.parametrize("eps", [0.01, 0.1])
+def test_sparsemixer_matches_reference(D, golden, name, eps):
+    """mb_router_sparsemixer against moelan's route_sparsemixer on the
+    reference's own near-tie / negative / zero case: picks bit-exact (they
+    come from the logits alone), weights within 2e-6 relative."""
+    lg = C.sparsemixer_inputs()[name]
+    idx, w = D.router_sparsemixer(cu(lg), eps)
+    assert np.array_equal(idx.cpu().numpy(), golden[f"sparse_{name}_{eps}_idx"])
+    np.testing.assert_allclose(w.cpu().numpy(), golden[f"sparse_{name}_{eps}_w"], rtol=2e-6, atol=1e-12)
+    assert (golden[f"sparse_{name}_{eps}_w"] < 0.999).any()
+
+
+def test_grouped_router_large_batch(D):
+    """DeepSeek-V3 routing (256 experts, 8 groups, keep 4, top-8) at prefill
+    size against the numpy restatement."""
+    rng = np.random.default_rng(99)
+    T, E = 4096, 256
+    lg = rng.standard_normal((T, E)).astype(np.float32)
+    bias = (rng.standard_normal(E) * 0.05).astype(np.float32)
+    idx, w = D.router_grouped(cu(lg), 8, "sigmoid", "noaux_tc", 8, 4, True, 2.5, cu(bias))
+    want_i, want_w, choice = O.route_grouped(lg, 8, "sigmoid", "noaux_tc", 8, 4, True, 2.5, bias)
+    ok = ~_near_ties(choice, 8)
+    assert ok.mean() > 0.99
+    assert np.array_equal(idx.cpu().numpy()[ok], want_i[ok])
+    np.testing.assert_allclose(w.cpu().numpy()[ok], want_w[ok], rtol=2e-6, atol=1e-12)

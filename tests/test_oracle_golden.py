@@ -142,3 +142,22 @@ def test_wire_rows_bit_exact(golden, name, wire):
         assert np.array_equal(s.view(np.uint32), golden[f"wire_{name}_{wire}_s"].view(np.uint32))
     dec = O.decode_rows(q, s)
     assert np.array_equal(dec.view(np.uint32), golden[f"wire_{name}_{wire}_dec"].view(np.uint32))
+
+
+@pytest.mark.parametrize("case", C.GROUPED_CASES, ids=[c[0] for c in C.GROUPED_CASES])
+def test_grouped_router_bit_exact(golden, case):
+    """DeepSeek grouped routing restated in numpy against moelan's route_grouped."""
+    name, T, E, k, scoring, method, ng, tg, norm, scale, with_bias, seed = case
+    lg, bias = C.grouped_inputs(T, E, with_bias, seed)
+    idx, w, _ = O.route_grouped(lg, k, scoring, method, ng, tg, norm, scale, bias)
+    assert np.array_equal(idx, golden[f"grouped_{name}_idx"])
+    assert np.array_equal(w.view(np.uint32), golden[f"grouped_{name}_w"].view(np.uint32))
+
+
+@pytest.mark.parametrize("name", ["hf", "wide"])
+@pytest.mark.parametrize("eps", [0.01, 0.1])
+def test_sparsemixer_bit_exact(golden, name, eps):
+    lg = C.sparsemixer_inputs()[name]
+    idx, w = O.route_sparsemixer(lg, eps)
+    assert np.array_equal(idx, golden[f"sparse_{name}_{eps}_idx"])
+    assert np.array_equal(w.view(np.uint32), golden[f"sparse_{name}_{eps}_w"].view(np.uint32))
