@@ -19,6 +19,10 @@ SIGNATURES = {
     "mb_last_error": (ctypes.c_char_p, []),
     "mb_version": (_int, []),
     "mb_device_check": (_int, []),
+    "mb_tiles_bytes": (_i64, [_int, _int, _int, _int]),
+    "mb_pack_q4": (_int, [_vp, _vp, _int, _int, _int, _int, _u8, _int, _vp, _vp]),
+    "mb_pack_q8": (_int, [_vp, _vp, _int, _int, _int, _int, _int, _vp, _vp]),
+    "mb_pack_q4k": (_int, [_vp, _int, _int, _int, _vp, _vp]),
     "mb_q4_dequant": (_int, [_vp, _vp, _int, _i64, _i64, _int, _u8, _vp, _vp]),
     "mb_q8_dequant": (_int, [_vp, _vp, _int, _i64, _i64, _int, _vp, _vp]),
     "mb_gguf_dequant": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _vp]),

@@ -40,6 +40,45 @@ def require_device() -> None:
         _checked_devices.add(dev)
 
 
+# ---- the tile layout, made on the device ----------------------------------------------
+
+def tiles_bytes(fmt: int, O: int, K: int, inter: int = 0) -> int:
+    return int(lib().mb_tiles_bytes(int(fmt), O, K, inter))
+
+
+def pack_q4(raw: torch.Tensor, s: torch.Tensor, gs: int, offset: bool, inter: int = 0, out: torch.Tensor | None = None):
+    """Tiles of colibri int4 bytes raw (O, K/2) with scales s (O, K/gs) f16 or f32."""
+    _cuda(raw, s, out)
+    O, K = raw.shape[0], 2 * raw.shape[1]
+    f16 = s.dtype == torch.float16
+    n = tiles_bytes(2 if f16 else 1, O, K, inter)
+    out = torch.empty(n, dtype=torch.uint8, device=raw.device) if out is None else out
+    check(lib().mb_pack_q4(_p(raw), _p(s), int(f16), O, K, gs, 0 if offset else 0x88, inter, _p(out), _stream()),
+          "mb_pack_q4")
+    return out
+
+
+def pack_q8(q: torch.Tensor, s: torch.Tensor, gs: int, inter: int = 0, out: torch.Tensor | None = None):
+    """Tiles of group-scaled int8 q (O, K) with scales s (O, K/gs) f16 or f32."""
+    _cuda(q, s, out)
+    O, K = q.shape
+    f16 = s.dtype == torch.float16
+    n = tiles_bytes(4 if f16 else 3, O, K, inter)
+    out = torch.empty(n, dtype=torch.uint8, device=q.device) if out is None else out
+    check(lib().mb_pack_q8(_p(q), _p(s), int(f16), O, K, gs, inter, _p(out), _stream()), "mb_pack_q8")
+    return out
+
+
+def pack_q4k(raw: torch.Tensor, K: int, inter: int = 0, out: torch.Tensor | None = None):
+    """Affine int4 tiles of GGUF Q4_K rows raw (O, K/256 * 144)."""
+    _cuda(raw, out)
+    O = raw.shape[0]
+    n = tiles_bytes(5, O, K, inter)
+    out = torch.empty(n, dtype=torch.uint8, device=raw.device) if out is None else out
+    check(lib().mb_pack_q4k(_p(raw), O, K, inter, _p(out), _stream()), "mb_pack_q4k")
+    return out
+
+
 # ---- dequantisation ----------------------------------------------------------------
 
 def q4_dequant(raw: torch.Tensor, s: torch.Tensor, gs: int, offset: bool, out: torch.Tensor | None = None):

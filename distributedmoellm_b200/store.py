@@ -18,6 +18,12 @@ from . import layout
 ALIGN = 256
 
 
+def _up(a, dev) -> torch.Tensor:
+    """A host array (or tensor) as a contiguous tensor on dev."""
+    t = a if isinstance(a, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(a))
+    return t.to(dev).contiguous()
+
+
 def _al(n: int) -> int:
     return (n + ALIGN - 1) // ALIGN * ALIGN
 
@@ -65,6 +71,11 @@ class LayerExperts:
             if src.numel() != n:
                 raise ValueError(f"tile bytes {src.numel()} != expected {n}")
             self.buf[off:off + n].copy_(src.reshape(-1), non_blocking=False)
+        self._place(e, eexp)
+
+    def _place(self, e: int, eexp) -> None:
+        """Record expert e's slot addresses and exponents after its tiles are written."""
+        g0, d0 = self._slot(e)
         base = self.buf.data_ptr()
         self._table_host[e] = (base + g0, base + d0)
         if eexp is None:
@@ -75,17 +86,39 @@ class LayerExperts:
             self.missing_exp.discard(e)
         self.present.add(e)
 
+    def _check_fmt(self, kind: str, s_gu, s_dn) -> None:
+        if layout.fmt_of(kind, s_gu) != self.fmt_gu or layout.fmt_of(kind, s_dn) != self.fmt_down:
+            raise ValueError(f"{kind} expert with {np.asarray(s_gu).dtype} / {np.asarray(s_dn).dtype} scales does "
+                             f"not match this layer's formats {self.fmt_gu} / {self.fmt_down}")
+
     def put_int4(self, e: int, gu_raw, gu_s, dn_raw, dn_s, offset: bool = False) -> None:
-        """Expert ``e`` from colibri int4 arrays (moelan Packed4: raw, s)."""
-        self.put_tiles(e, layout.q4_tiles(gu_raw, gu_s, self.gs, offset, gu_inter=self.I),
-                       layout.q4_tiles(dn_raw, dn_s, self.gs, offset),
-                       (layout.weight_exponent(gu_s, 8), layout.weight_exponent(dn_s, 8),
+        """Expert ``e`` from colibri int4 arrays (moelan Packed4: raw, s), laid
+        out into its slot on the device (mb_pack_q4) from the bytes as they are."""
+        from . import device as D
+        if e not in self.slot_of:
+            raise KeyError(f"expert {e} is not placed on this device")
+        self._check_fmt("q4", gu_s, dn_s)
+        g0, d0 = self._slot(e)
+        dev = self.device
+        with torch.cuda.device(dev):
+            D.pack_q4(_up(gu_raw, dev), _up(gu_s, dev), self.gs, offset, self.I, out=self.buf[g0:g0 + self.gu_nbytes])
+            D.pack_q4(_up(dn_raw, dev), _up(dn_s, dev), self.gs, offset, 0, out=self.buf[d0:d0 + self.dn_nbytes])
+        self._place(e, (layout.weight_exponent(gu_s, 8), layout.weight_exponent(dn_s, 8),
                         layout.act_exponent(layout.row_l1_q4(gu_raw, gu_s, self.gs, offset), self.I)))
 
     def put_int8(self, e: int, gu_q, gu_s, dn_q, dn_s) -> None:
-        """Expert ``e`` from group-scaled int8 arrays (moelan GroupQuant: q, s)."""
-        self.put_tiles(e, layout.q8_tiles(gu_q, gu_s, self.gs, gu_inter=self.I), layout.q8_tiles(dn_q, dn_s, self.gs),
-                       (layout.weight_exponent(gu_s, 128), layout.weight_exponent(dn_s, 128),
+        """Expert ``e`` from group-scaled int8 arrays (moelan GroupQuant: q, s),
+        laid out into its slot on the device (mb_pack_q8)."""
+        from . import device as D
+        if e not in self.slot_of:
+            raise KeyError(f"expert {e} is not placed on this device")
+        self._check_fmt("q8", gu_s, dn_s)
+        g0, d0 = self._slot(e)
+        dev = self.device
+        with torch.cuda.device(dev):
+            D.pack_q8(_up(gu_q, dev), _up(gu_s, dev), self.gs, self.I, out=self.buf[g0:g0 + self.gu_nbytes])
+            D.pack_q8(_up(dn_q, dev), _up(dn_s, dev), self.gs, 0, out=self.buf[d0:d0 + self.dn_nbytes])
+        self._place(e, (layout.weight_exponent(gu_s, 128), layout.weight_exponent(dn_s, 128),
                         layout.act_exponent(layout.row_l1_q8(gu_q, gu_s, self.gs), self.I)))
 
     def put_expert(self, e: int, expert) -> None:

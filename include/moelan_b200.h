@@ -58,6 +58,32 @@ int mb_version(void);
 /* MB_OK when the current device is an sm_100 part this build runs on. */
 int mb_device_check(void);
 
+/* ---- the device tile layout, made on the device ----------------------------- */
+
+/* Bytes of one matrix (O rows, K columns) in the tile layout of format fmt;
+ * inter > 0 for a gate|up matrix of 2 * inter rows.  -1 for a bad argument. */
+int64_t mb_tiles_bytes(int fmt, int O, int K, int inter);
+
+/* Tiles (MB_FMT_Q4_F16 when scale_f16, else MB_FMT_Q4_F32) from moelan's int4
+ * bytes as they are (moelan/experts.py:170-236 Packed4: raw (O, K/2), scales
+ * (O, K/gs); xor_mask 0x88 for two's-complement nibbles, 0 for the XOR-ed
+ * resident form, as mb_q4_dequant), so a caller holding those arrays needs no
+ * host re-layout.  Byte-identical to the layout distributedmoellm_b200/layout.py
+ * writes.  tiles: mb_tiles_bytes(fmt, O, K, inter) bytes, 16-byte aligned. */
+int mb_pack_q4(const uint8_t *raw, const void *scales, int scale_f16, int O, int K, int gs, uint8_t xor_mask,
+               int inter, void *tiles, void *stream);
+
+/* Tiles (MB_FMT_Q8_F16 / MB_FMT_Q8_F32) from moelan's GroupQuant int8 (q (O, K),
+ * scales (O, K/gs); moelan/experts.py:125-167), or from GGUF Q8_0 values and
+ * their f16 block scales. */
+int mb_pack_q8(const int8_t *q, const void *scales, int scale_f16, int O, int K, int gs, int inter, void *tiles,
+               void *stream);
+
+/* Affine int4 tiles (MB_FMT_Q4K_F32) from GGUF Q4_K rows as stored (O rows of
+ * K/256 144-byte super-blocks; moelan/kernels.py:310-336): nibbles q, scales
+ * d*sc, biases 8*d*sc - dmin*m. */
+int mb_pack_q4k(const uint8_t *raw, int O, int K, int inter, void *tiles, void *stream);
+
 /* ---- dequantisation (bit-exact) -------------------------------------------- */
 
 /* moelan/kernels.py:971 q4_dequant(raw, s, gs, offset, out) -> _q4_dequant

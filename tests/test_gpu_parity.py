@@ -518,3 +518,42 @@ def test_grouped_router_large_batch(D):
     assert ok.mean() > 0.99
     assert np.array_equal(idx.cpu().numpy()[ok], want_i[ok])
     np.testing.assert_allclose(w.cpu().numpy()[ok], want_w[ok], rtol=2e-6, atol=1e-12)
+
+
+# ---- the tile layout made on the device -------------------------------------------------
+
+@pytest.mark.parametrize("O,K,gs,inter", [(96, 256, 32, 0), (33, 384, 64, 0), (2 * 52, 512, 32, 52),
+                                          (1536, 2048, 32, 768), (2048, 768, 32, 0)])
+@pytest.mark.parametrize("f16", [False, True])
+def test_pack_matches_host_layout(D, O, K, gs, inter, f16):
+    """mb_pack_q4 / mb_pack_q8 write byte for byte what layout.q4_tiles /
+    q8_tiles write, both nibble forms, plain and gate|up matrices, ragged rows."""
+    from distributedmoellm_b200 import layout as L
+    rng = np.random.default_rng(O + K)
+    raw = rng.integers(0, 256, (O, K // 2), dtype=np.uint8)
+    s = rng.random((O, K // gs), dtype=np.float32)
+    if f16:
+        s = s.astype(np.float16)
+    for offset in (False, True):
+        got = D.pack_q4(cu(raw), cu(s), gs, offset, inter).cpu().numpy()
+        assert np.array_equal(got, L.q4_tiles(raw, s, gs, offset, gu_inter=inter))
+    q = rng.integers(-127, 128, (O, K), dtype=np.int8)
+    got = D.pack_q8(cu(q), cu(s), gs, inter).cpu().numpy()
+    assert np.array_equal(got, L.q8_tiles(q, s, gs, gu_inter=inter))
+
+
+@pytest.mark.parametrize("O,K,inter", [(40, 512, 0), (2 * 56, 1024, 56), (4096, 256, 0)])
+def test_pack_q4k_matches_host_layout(D, O, K, inter):
+    """mb_pack_q4k against layout.q4k_tiles on random Q4_K rows: every packed
+    scale / min code, f16 d and dmin finite (normal and subnormal; an infinite
+    d makes NaN biases, whose bit pattern differs between numpy and CUDA)."""
+    from distributedmoellm_b200 import layout as L
+    rng = np.random.default_rng(O)
+    raw = rng.integers(0, 256, (O, K // 256, 144), dtype=np.uint8)
+    dd = (rng.standard_normal((O, K // 256, 2)) * 0.01).astype(np.float16)
+    dd[::7, :, 0] = np.float16(3e-6)                      # subnormal d
+    raw[:, :, 0:4] = dd.view(np.uint8).reshape(O, K // 256, 4)
+    raw = raw.reshape(O, K // 256 * 144)
+    got = D.pack_q4k(cu(raw), K, inter).cpu().numpy()
+    want = L.q4k_tiles(raw, K, gu_inter=inter)
+    assert np.array_equal(got, want)
