@@ -69,6 +69,8 @@ def parse():
     p.add_argument("--no-prefill", action="store_true")
     p.add_argument("--no-dropin", action="store_true", help="skip the drop-in moe_q4 end-to-end figure")
     p.add_argument("--no-parity", action="store_true", help="skip the multi-GPU step's check against one GPU")
+    p.add_argument("--phases", action="store_true",
+                   help="with --gpus N > 1: time each phase of the expert-parallel decode step (eager, CUDA events)")
     return p.parse_args()
 
 
@@ -415,6 +417,7 @@ def run_gpu_ep(args, rank, world, dev):
         parity["decode"] = ep_parity(layers[0], lambda: MoELayer(rt, full, K_TOP, True, gemm_min_rows=0),
                                      T, rank, world, dev, 2e-3 if ep_gemm else 1e-5, 4000)
         del full
+    phases = ep_phase_times(layers[0], T, rank, dev, 50, 5) if args.phases else None
     gpu_index = dev.index or 0
     with Clocks(gpu_index) as clk:
         ms = measure(layers, T, args.steps, args.warmup, 1000, graphs=True)
@@ -455,7 +458,38 @@ def run_gpu_ep(args, rank, world, dev):
                                                "ms_per_step": round(m, 5)}
     if parity:
         prefill["parity"] = parity
+    if phases:
+        prefill["decode_phases_us"] = phases
     return value, ms, roof, e2e, {}, None, clk.summary(), 0, prefill, None
+
+
+def ep_phase_times(layer, T, rank, dev, steps, warmup):
+    """Per-phase device time of the expert-parallel decode step (eager
+    launches, CUDA events recorded between the phases on the current stream),
+    the mean over ``steps`` steps, then the max over ranks, in microseconds."""
+    import torch
+    import torch.distributed as dist
+    x = torch.from_numpy(np.random.default_rng(77 + rank).standard_normal((T, H), dtype=np.float32)).to(dev)
+    names = ["gather", "route", "permute", "experts", "combine", "reduce"]
+    tot = {n: 0.0 for n in names}
+    for it in range(warmup + steps):
+        ev = {"start": torch.cuda.Event(enable_timing=True)}
+        ev["start"].record()
+
+        def mark(name):
+            ev[name] = torch.cuda.Event(enable_timing=True)
+            ev[name].record()
+        layer(x, mark=mark)
+        torch.cuda.synchronize()
+        if it >= warmup:
+            prev = "start"
+            for n in names:
+                tot[n] += ev[prev].elapsed_time(ev[n]) * 1e3
+                prev = n
+    dist.barrier()
+    t = torch.tensor([tot[n] / steps for n in names], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return {n: round(float(v), 2) for n, v in zip(names, t.tolist())}
 
 
 def ep_parity(ep_layer, make_full, T, rank, world, dev, bar, seed):

@@ -216,22 +216,32 @@ class EPGatherLayer:
             b = self._bufs[T] = _GatherBuffers(T, self.world, self.E, self.k, ex.H, ex.I, self.router.device)
         return b
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, mark=None) -> torch.Tensor:
+        """``mark(name)``, when given, is called after each phase (gather,
+        route, permute, experts, combine, reduce) on the host as the phase's
+        work is enqueued, e.g. to record CUDA events between the phases."""
+        mark = mark or (lambda name: None)
         T = x.shape[0]
         b = self.buffers(T)
         e0, El, k = self.first_expert, self.E_local, self.k
         dist.all_gather_into_tensor(b.x_all, x.contiguous(), group=self.group)
+        mark("gather")
         D.router_route(b.x_all, self.router, k, self.normalize, b.idx, b.w, row_exp=b.row_exp, workspace=b.rws)
+        mark("route")
         r = D.permute(b.idx, b.w, self.E, b.routing)
+        mark("permute")
         P = r.P
         local = D.Routing.from_plan(r.counts[e0:e0 + El], r.offsets[e0:e0 + El + 1], r.sorted_rows[:P])
         run_experts(self.experts, b.x_all, b.row_exp, local, b.y, b.workspace, b.status, self.gemm_min_rows,
                     picks=P // self.world)
+        mark("experts")
         # the other ranks' picks are skipped by the combine (pick index -1)
         mine = (b.idx.view(-1) >= e0) & (b.idx.view(-1) < e0 + El)
         torch.where(mine, r.inv[:P], torch.full_like(r.inv[:P], -1), out=b.inv_local[:P])
         D.combine(b.y, b.inv_local[:P], b.w.view(-1), T * self.world, k, out=b.partial)
+        mark("combine")
         dist.reduce_scatter_tensor(b.out, b.partial, group=self.group)
+        mark("reduce")
         return b.out
 
     __call__ = forward
