@@ -22,7 +22,7 @@ import numpy as np
 import torch
 
 from . import device as D
-from .layer import run_experts
+from .layer import GEMM_MIN_ROWS, run_experts
 from .packing import pack_expert
 
 
@@ -68,7 +68,7 @@ class DevicePool:
                 b = self._ws[name] = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=self.device)
             return b
 
-    def compute(self, x: torch.Tensor, keys, rows, weights, gemm_min_rows: int = 32):
+    def compute(self, x: torch.Tensor, keys, rows, weights, gemm_min_rows: int = GEMM_MIN_ROWS):
         """Weighted expert outputs summed per input row: returns (unique rows,
         (U, H) device tensor) with sum_p w_p * expert_p(x[row_p]) for the picks
         (keys[i], rows[i][j], weights[i][j])."""

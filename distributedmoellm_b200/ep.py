@@ -39,7 +39,7 @@ import torch
 import torch.distributed as dist
 
 from . import device as D
-from .layer import run_experts
+from .layer import GEMM_MIN_ROWS, run_experts
 
 
 def local_plan(recv_ec: np.ndarray):
@@ -116,7 +116,7 @@ class DeviceOps:
     0 .. E/G-1 (global id = rank * E/G + local id)."""
 
     def __init__(self, router: torch.Tensor, experts, E: int, top_k: int, normalize: bool = True,
-                 gemm_min_rows: int = 32):
+                 gemm_min_rows: int = GEMM_MIN_ROWS):
         self.router = router.contiguous()
         self.store = experts
         self.E, self.k, self.normalize = E, top_k, normalize
@@ -197,7 +197,7 @@ class EPGatherLayer:
     one-GPU layer's up to the order of the final sum over ranks."""
 
     def __init__(self, router: torch.Tensor, experts, E: int, top_k: int, normalize: bool = True, group=None,
-                 gemm_min_rows: int = 32):
+                 gemm_min_rows: int = GEMM_MIN_ROWS):
         self.router = router.contiguous()
         self.experts, self.E, self.k, self.normalize, self.group = experts, E, top_k, normalize, group
         self.world = dist.get_world_size(group)

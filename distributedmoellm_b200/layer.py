@@ -16,28 +16,31 @@ import torch
 from . import device as D
 from .store import LayerExperts
 
+# average picks per expert from which a layer's experts run as grouped GEMMs (see kernel_plan)
+GEMM_MIN_ROWS = 8
+
 
 def uses_gemm(experts: LayerExperts, P: int, gemm_min_rows: int) -> bool:
-    """Whether the grouped-GEMM kernels run for P picks over these experts:
-    only when the picks average at least half of gemm_min_rows per expert
-    (prefill-sized batches) and the shape allows them (H % 128, I % 64)."""
+    """Whether the grouped-GEMM kernels take the experts' P picks: once the
+    picks average at least gemm_min_rows per expert (and the shape allows
+    them: H % 128, I % 64, P <= 65536; experts stored without the tensor-core
+    exponents stay on the decode kernels)."""
     m = gemm_min_rows
-    return (m > 0 and experts.H % 128 == 0 and experts.I % 64 == 0 and 2 * P >= experts.E * m
-            and P <= 65536 and not experts.missing_exp)
+    return (m > 0 and experts.H % 128 == 0 and experts.I % 64 == 0 and P >= experts.E * m and P <= 65536
+            and not experts.missing_exp)
 
 
 def kernel_plan(experts, P: int, gemm_min_rows: int) -> list:
-    """Which kernels run for P picks over these experts, in launch order:
-    ("decode", max_rows) and / or ("gemm", min_rows).  The GEMM runs only for
-    prefill-sized batches (see uses_gemm), over every expert once the picks
-    average twice gemm_min_rows (the decode launches would mostly find nothing
-    to do), else over the experts with at least gemm_min_rows picks with the
-    rest on the decode kernels."""
-    if uses_gemm(experts, P, gemm_min_rows):
-        if P >= 2 * experts.E * gemm_min_rows:
-            return [("gemm", 1)]
-        return [("decode", gemm_min_rows - 1), ("gemm", gemm_min_rows)]
-    return [("decode", 0)]
+    """Which kernels run for P picks over these experts: ("gemm", 1), every
+    expert as a grouped GEMM, or ("decode", 0), every expert on the decode
+    mat-vecs.  Timed on B200 at the Qwen3-30B shape (expert kernels, graph
+    replays): 128 experts at 1024 / 2048 / 4096 picks take 170 / 172 / 180 us
+    as GEMMs against 163 / 266 / 473 us decoded, and a 16-expert slice with 512
+    picks 46 us against 88 us; splitting a layer between the two (experts
+    below some pick count decoded, the rest as GEMMs) was never faster than the
+    better of the two (96, 257-282, 355 us), so one of them takes every
+    expert, the GEMM from 8 picks per expert on average."""
+    return [("gemm", 1)] if uses_gemm(experts, P, gemm_min_rows) else [("decode", 0)]
 
 
 def run_experts(experts: LayerExperts, x: torch.Tensor, row_exp: torch.Tensor, routing, y: torch.Tensor,
@@ -79,16 +82,15 @@ class _Buffers:
 class MoELayer:
     """``router`` (E, H) f32 on the device; ``experts`` the layer's packed experts.
 
-    Experts picked by at least ``gemm_min_rows`` tokens run as grouped GEMMs
-    on the tensor cores (f16 operands, f32 accumulation; the reference's
-    dense path for 8 or more rows, experts.py:148-151, 216-219), the rest
-    through the f32-exact decode mat-vecs.  The GEMM kernels are launched
-    only when the layer's picks average at least half that many per expert
-    (prefill-sized batches) and the shape allows them (H % 128, I % 64);
-    ``gemm_min_rows=0`` keeps every expert on the decode kernels."""
+    Once the layer's picks average ``gemm_min_rows`` per expert (prefill-sized
+    batches) every expert runs as a grouped GEMM on the tensor cores (f16
+    operands, f32 accumulation; the reference's dense path for 8 or more
+    rows, experts.py:148-151, 216-219), below that through the f32-exact
+    decode mat-vecs (see kernel_plan); ``gemm_min_rows=0`` keeps every expert
+    on the decode kernels."""
 
     def __init__(self, router: torch.Tensor, experts: LayerExperts, top_k: int, normalize: bool = True,
-                 gemm_min_rows: int = 32):
+                 gemm_min_rows: int = GEMM_MIN_ROWS):
         self.router = router.contiguous()
         self.experts = experts
         self.E, self.H, self.I = experts.E, experts.H, experts.I

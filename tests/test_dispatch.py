@@ -1,9 +1,8 @@
-"""The layer's choice of kernels (layer.run_experts), on CPU with the device
-entry points replaced by recorders: the decode mat-vecs for small batches,
-both kernels for mid-sized ones (experts below gemm_min_rows picks on the
-decode kernel), every expert on the grouped GEMM once the picks average twice
-gemm_min_rows, for every weight format and size (affine int4, K > 2048
-included)."""
+"""The layer's choice of kernels (layer.kernel_plan / run_experts), on CPU
+with the device entry points replaced by recorders: every expert on the
+decode mat-vecs below GEMM_MIN_ROWS picks per expert on average, every expert
+as a grouped GEMM from there on, for every weight format and size (affine
+int4, K > 2048 included), never a split between the two."""
 
 import sys
 import types
@@ -23,7 +22,7 @@ def _experts(E=128, H=2048, I=768, fmt=L.FMT_Q4_F16):
                                  missing_exp=False)
 
 
-def _run(monkeypatch, ex, P, picks=None, m=32):
+def _run(monkeypatch, ex, P, picks=None, m=Lyr.GEMM_MIN_ROWS):
     calls = []
     monkeypatch.setattr(Lyr.D, "moe_decode", lambda *a, **k: calls.append(("decode", k.get("max_rows"))))
     monkeypatch.setattr(Lyr.D, "moe_prefill", lambda *a, **k: calls.append(("gemm", k.get("min_rows"))))
@@ -35,9 +34,10 @@ def _run(monkeypatch, ex, P, picks=None, m=32):
 
 
 @pytest.mark.parametrize("T,want", [
-    (64, [("decode", 0)]),                               # decode batch: 512 picks over 128 experts
-    (256, [("decode", 31), ("gemm", 32)]),               # 2048 picks: 16 per expert on average
-    (1024, [("gemm", 1)]),                               # 8192 picks: 64 per expert, all on the GEMM
+    (1, [("decode", 0)]),
+    (64, [("decode", 0)]),       # 512 picks over 128 experts: 4 per expert
+    (127, [("decode", 0)]),
+    (128, [("gemm", 1)]),        # 1024 picks: 8 per expert
     (2048, [("gemm", 1)]),
 ])
 def test_kernel_choice_by_batch(monkeypatch, T, want):
@@ -54,9 +54,14 @@ def test_affine_and_wide_experts_follow_the_batch(monkeypatch):
 def test_expert_parallel_slice_decides_by_its_own_picks(monkeypatch):
     # a rank's 16 experts out of 128 see all ranks' picks in the routing; the choice follows its share
     ex = _experts(E=16)
-    assert _run(monkeypatch, ex, 4096, picks=512) == [("decode", 31), ("gemm", 32)]
-    assert _run(monkeypatch, ex, 4096, picks=255) == [("decode", 0)]   # below 16 per expert on average
-    assert _run(monkeypatch, ex, 16384, picks=2048) == [("gemm", 1)]
+    assert _run(monkeypatch, ex, 4096, picks=512) == [("gemm", 1)]    # 8 ranks x 64 tokens: 32 per expert
+    assert _run(monkeypatch, ex, 4096, picks=127) == [("decode", 0)]  # below 8 per expert on average
+
+
+def test_shapes_the_gemm_cannot_take_stay_on_decode(monkeypatch):
+    assert _run(monkeypatch, _experts(H=1000), 65536) == [("decode", 0)]   # H % 128
+    assert _run(monkeypatch, _experts(I=96), 65536) == [("decode", 0)]     # I % 64
+    assert _run(monkeypatch, _experts(), 4096, m=0) == [("decode", 0)]     # gemm_min_rows=0
 
 
 def test_experts_without_exponents_stay_on_the_decode_kernels(monkeypatch):
@@ -70,4 +75,4 @@ def test_experts_without_exponents_stay_on_the_decode_kernels(monkeypatch):
 def test_largest_permutation_reaches_the_gemm(monkeypatch):
     # mb_permute takes up to 65536 picks (T=8192, k=8) and so does the grouped GEMM
     assert _run(monkeypatch, _experts(fmt=L.FMT_Q4K_F32), 65536) == [("gemm", 1)]
-    assert _run(monkeypatch, _experts(), 65536) == [("gemm", 1)]
+    assert _run(monkeypatch, _experts(), 65537) == [("decode", 0)]

@@ -289,11 +289,11 @@ def _check_gguf_layer(layer, desc, x, I):
 
 
 def test_gguf_q4_k_layer_matches_oracle(D):
-    """Q4_K gate|up + Q8_0 down: the affine int4 decode kernel at 1 and 24
+    """Q4_K gate|up + Q8_0 down: the affine int4 decode kernel at 1 and 12
     tokens (1e-5), the grouped GEMM at 300 (2e-3)."""
     rng = np.random.default_rng(12)
     layer, desc = _gguf_layer(rng, 4, 512, 256, 2)
-    for T in (1, 24, 300):
+    for T in (1, 12, 300):
         assert layer.uses_gemm(T) == (T == 300)
         _check_gguf_layer(layer, desc, rng.standard_normal((T, 512), dtype=np.float32), 256)
 
