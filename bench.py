@@ -470,7 +470,7 @@ def ep_phase_times(layer, T, rank, dev, steps, warmup):
     import torch
     import torch.distributed as dist
     x = torch.from_numpy(np.random.default_rng(77 + rank).standard_normal((T, H), dtype=np.float32)).to(dev)
-    names = ["gather", "route", "permute", "experts", "combine", "reduce"]
+    names = ["route", "gather", "permute", "experts", "combine", "reduce"]
     tot = {n: 0.0 for n in names}
     for it in range(warmup + steps):
         ev = {"start": torch.cuda.Event(enable_timing=True)}

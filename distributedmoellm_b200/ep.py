@@ -24,12 +24,13 @@ other ops over gloo on CPU.
 
 ``EPGatherLayer`` is the form for decode-sized batches, where the host round
 trip of the exchange plan would cost more than the experts: every rank
-all-gathers the tokens, routes all of them (the same kernels on the same
-data give every rank the same routing), runs its own expert slice over the
-picks that fall in it, sums each token's local picks (the other picks are
-skipped) and a reduce-scatter adds the ranks' partial sums.  All sizes are
-fixed by T, nothing goes through the host, and the step can be captured in a
-CUDA graph, collectives included.
+routes its own tokens, all-gathers the tokens together with their routing
+(one NCCL group of four gathers), sorts all ranks' picks by expert (the same
+kernel on the same data gives every rank the same order), runs its own
+expert slice over the picks that fall in it, sums each token's local picks
+(the other picks are skipped) and a reduce-scatter adds the ranks' partial
+sums.  All sizes are fixed by T, nothing goes through the host, and the step
+can be captured in a CUDA graph, collectives included.
 """
 
 from __future__ import annotations
@@ -173,8 +174,12 @@ class _GatherBuffers:
         self.row_exp = torch.empty(TA, dtype=torch.int32, device=dev)
         self.idx = torch.empty((TA, k), dtype=torch.int32, device=dev)
         self.w = torch.empty((TA, k), dtype=torch.float32, device=dev)
+        # this rank's own tokens' routing, gathered next to the tokens
+        self.row_exp_own = torch.empty(T, dtype=torch.int32, device=dev)
+        self.idx_own = torch.empty((T, k), dtype=torch.int32, device=dev)
+        self.w_own = torch.empty((T, k), dtype=torch.float32, device=dev)
         self.routing = D.Routing(TA, k, E, dev)
-        self.rws = torch.empty(D.router_workspace_bytes(TA, H, E), dtype=torch.uint8, device=dev)
+        self.rws = torch.empty(D.router_workspace_bytes(T, H, E), dtype=torch.uint8, device=dev)
         self.y = torch.empty((max(P, 1), H), dtype=torch.float32, device=dev)
         self.inv_local = torch.empty(max(P, 1), dtype=torch.int32, device=dev)
         self.partial = torch.empty((TA, H), dtype=torch.float32, device=dev)
@@ -191,7 +196,8 @@ class _GatherBuffers:
 
 class EPGatherLayer:
     """One MoE layer over the ranks of ``group`` for decode-sized batches:
-    all-gather of the tokens, replicated routing, the rank's own experts
+    each rank routes its own tokens, all-gather of the tokens with their
+    routing, the rank's own experts
     (``experts``: its E/G local experts as local ids 0 .. E/G-1), combine of
     its picks, reduce-scatter of the partial sums.  Token results equal the
     one-GPU layer's up to the order of the final sum over ranks."""
@@ -217,17 +223,23 @@ class EPGatherLayer:
         return b
 
     def forward(self, x: torch.Tensor, mark=None) -> torch.Tensor:
-        """``mark(name)``, when given, is called after each phase (gather,
-        route, permute, experts, combine, reduce) on the host as the phase's
+        """``mark(name)``, when given, is called after each phase (route,
+        gather, permute, experts, combine, reduce) on the host as the phase's
         work is enqueued, e.g. to record CUDA events between the phases."""
         mark = mark or (lambda name: None)
         T = x.shape[0]
         b = self.buffers(T)
         e0, El, k = self.first_expert, self.E_local, self.k
-        dist.all_gather_into_tensor(b.x_all, x.contiguous(), group=self.group)
-        mark("gather")
-        D.router_route(b.x_all, self.router, k, self.normalize, b.idx, b.w, row_exp=b.row_exp, workspace=b.rws)
+        x = x.contiguous()
+        # each rank routes its own tokens; the tokens and their routing are gathered in one NCCL group
+        D.router_route(x, self.router, k, self.normalize, b.idx_own, b.w_own, row_exp=b.row_exp_own, workspace=b.rws)
         mark("route")
+        with dist._coalescing_manager(group=self.group, device=x.device):
+            dist.all_gather_into_tensor(b.x_all, x, group=self.group)
+            dist.all_gather_into_tensor(b.idx, b.idx_own, group=self.group)
+            dist.all_gather_into_tensor(b.w, b.w_own, group=self.group)
+            dist.all_gather_into_tensor(b.row_exp, b.row_exp_own, group=self.group)
+        mark("gather")
         r = D.permute(b.idx, b.w, self.E, b.routing)
         mark("permute")
         P = r.P
