@@ -17,7 +17,7 @@ from . import device as D
 from .store import LayerExperts
 
 # average picks per expert from which a layer's experts run as grouped GEMMs (see kernel_plan)
-GEMM_MIN_ROWS = 8
+GEMM_MIN_ROWS = 12
 
 
 def uses_gemm(experts: LayerExperts, P: int, gemm_min_rows: int) -> bool:
@@ -39,7 +39,9 @@ def kernel_plan(experts, P: int, gemm_min_rows: int) -> list:
     picks 46 us against 88 us; splitting a layer between the two (experts
     below some pick count decoded, the rest as GEMMs) was never faster than the
     better of the two (96, 257-282, 355 us), so one of them takes every
-    expert, the GEMM from 8 picks per expert on average."""
+    expert: the GEMM from 12 picks per expert on average (at 8 the two are
+    even on one GPU and the decode kernel measured ahead in a 2-GPU
+    expert-parallel step, where each rank's 64 experts get 8 picks)."""
     return [("gemm", 1)] if uses_gemm(experts, P, gemm_min_rows) else [("decode", 0)]
 
 

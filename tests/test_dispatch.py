@@ -1,6 +1,6 @@
 """The layer's choice of kernels (layer.kernel_plan / run_experts), on CPU
 with the device entry points replaced by recorders: every expert on the
-decode mat-vecs below GEMM_MIN_ROWS picks per expert on average, every expert
+decode mat-vecs below GEMM_MIN_ROWS (12) picks per expert on average, every expert
 as a grouped GEMM from there on, for every weight format and size (affine
 int4, K > 2048 included), never a split between the two."""
 
@@ -36,8 +36,9 @@ def _run(monkeypatch, ex, P, picks=None, m=Lyr.GEMM_MIN_ROWS):
 @pytest.mark.parametrize("T,want", [
     (1, [("decode", 0)]),
     (64, [("decode", 0)]),       # 512 picks over 128 experts: 4 per expert
-    (127, [("decode", 0)]),
-    (128, [("gemm", 1)]),        # 1024 picks: 8 per expert
+    (128, [("decode", 0)]),      # 1024 picks: 8 per expert
+    (191, [("decode", 0)]),
+    (192, [("gemm", 1)]),        # 1536 picks: 12 per expert
     (2048, [("gemm", 1)]),
 ])
 def test_kernel_choice_by_batch(monkeypatch, T, want):
@@ -55,7 +56,7 @@ def test_expert_parallel_slice_decides_by_its_own_picks(monkeypatch):
     # a rank's 16 experts out of 128 see all ranks' picks in the routing; the choice follows its share
     ex = _experts(E=16)
     assert _run(monkeypatch, ex, 4096, picks=512) == [("gemm", 1)]    # 8 ranks x 64 tokens: 32 per expert
-    assert _run(monkeypatch, ex, 4096, picks=127) == [("decode", 0)]  # below 8 per expert on average
+    assert _run(monkeypatch, ex, 4096, picks=191) == [("decode", 0)]  # below 12 per expert on average
 
 
 def test_shapes_the_gemm_cannot_take_stay_on_decode(monkeypatch):
