@@ -26,6 +26,9 @@ from .layer import GEMM_MIN_ROWS, run_experts
 from .packing import pack_expert
 
 
+_TORCH_DTYPE = {"<i4": torch.int32, "<i8": torch.int64, "<f4": torch.float32}
+
+
 class _Set:
     """Experts of one signature (formats, group size, H, I) passed to the kernels."""
 
@@ -43,6 +46,9 @@ class DevicePool:
         self.entries: dict = {}          # key -> (Packed, buffer, gu address, down address)
         self._ws: dict = {}
         self._ws_lock = threading.Lock()
+        self._pin = None            # pinned staging buffer of compute()'s routing arrays, and its device twin
+        self._dev_stage = None
+        self._stage_done = None     # recorded after the last copy out of the pinned buffer
 
     def put(self, key, packed) -> int:
         g = torch.from_numpy(np.ascontiguousarray(packed.gu_tiles))
@@ -68,48 +74,81 @@ class DevicePool:
                 b = self._ws[name] = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=self.device)
             return b
 
+    def _stage(self, arrays):
+        """Copy the given small host arrays to the device in one transfer through
+        a pinned staging buffer; returns device views of them in order.  Each
+        array starts on a 16-byte boundary and keeps its dtype."""
+        sizes = [(a.nbytes + 15) // 16 * 16 for a in arrays]
+        total = max(16, sum(sizes))
+        if self._pin is None or self._pin.numel() < total:
+            self._pin = torch.empty(max(total, 1 << 16), dtype=torch.uint8).pin_memory()
+            self._dev_stage = torch.empty(self._pin.numel(), dtype=torch.uint8, device=self.device)
+        if self._stage_done is not None:
+            self._stage_done.synchronize()     # the previous call's copy out of the pinned buffer has finished
+        host = self._pin.numpy()
+        off = 0
+        for a, n in zip(arrays, sizes):
+            host[off:off + a.nbytes] = np.ascontiguousarray(a).view(np.uint8).reshape(-1)
+            off += n
+        self._dev_stage[:total].copy_(self._pin[:total], non_blocking=True)
+        self._stage_done = torch.cuda.Event()
+        self._stage_done.record()
+        views, off = [], 0
+        for a, n in zip(arrays, sizes):
+            t = self._dev_stage[off:off + a.nbytes].view(_TORCH_DTYPE[a.dtype.str]).view(a.shape)
+            views.append(t)
+            off += n
+        return views
+
     def compute(self, x: torch.Tensor, keys, rows, weights, gemm_min_rows: int = GEMM_MIN_ROWS):
         """Weighted expert outputs summed per input row: returns (unique rows,
         (U, H) device tensor) with sum_p w_p * expert_p(x[row_p]) for the picks
-        (keys[i], rows[i][j], weights[i][j])."""
+        (keys[i], rows[i][j], weights[i][j]).  The call's routing arrays go to
+        the device in one copy; the kernels run on the current stream and the
+        result is ready when the stream reaches it (the caller's .cpu() waits)."""
         H = x.shape[1]
+        dev = self.device
         counts = np.array([len(r) for r in rows], np.int64)
         all_rows = np.concatenate([np.asarray(r, np.int64) for r in rows]) if len(rows) else np.zeros(0, np.int64)
         all_w = np.concatenate([np.asarray(w, np.float32) for w in weights]) if len(rows) else np.zeros(0, np.float32)
-        uniq, uidx = np.unique(all_rows, return_inverse=True)
         P = len(all_rows)
-        y = torch.empty((max(P, 1), H), dtype=torch.float32, device=self.device)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)     # this call's own status word
+        if P == 0:
+            return np.zeros(0, np.int64), torch.zeros((0, H), device=dev), status
+        uniq, uidx = np.unique(all_rows, return_inverse=True)
+        y = torch.empty((P, H), dtype=torch.float32, device=dev)
         row_exp = D.row_exponents(x)
-        status = torch.zeros(1, dtype=torch.int32, device=self.device)     # this call's own status word
         # experts of one signature share a launch
         sigs: dict = {}
         for i, k in enumerate(keys):
             sigs.setdefault(self.entries[k][0].signature, []).append(i)
         base = np.concatenate([[0], np.cumsum(counts)])
+        # per unique row, its picks in order: CSR for the weighted combine
+        order = np.argsort(uidx, kind="stable").astype(np.int32)
+        row_ptr = np.concatenate([[0], np.cumsum(np.bincount(uidx, minlength=len(uniq)))]).astype(np.int32)
+        host = [order, all_w[order], row_ptr]
+        plan = []
         for sig, idx in sigs.items():
             table = np.array([[self.entries[keys[i]][2], self.entries[keys[i]][3]] for i in idx], np.int64)
             eexp = np.zeros((len(idx), 4), np.int32)
             eexp[:, :3] = [self.entries[keys[i]][0].eexp for i in idx]
-            c = counts[idx]
+            c = counts[idx].astype(np.int32)
             sel = np.concatenate([np.arange(base[i], base[i + 1]) for i in idx])
-            dev = self.device
-            r = D.Routing.from_plan(torch.from_numpy(c.astype(np.int32)).to(dev),
-                                    torch.from_numpy(np.concatenate([[0], np.cumsum(c)]).astype(np.int32)).to(dev),
-                                    torch.from_numpy(all_rows[sel].astype(np.int32)).to(dev))
-            s = _Set(*sig, torch.from_numpy(table).to(dev), torch.from_numpy(eexp).to(dev))
-            if len(sigs) == 1:       # one signature (the usual case): its picks are all picks, in order
+            plan.append((sig, len(host), sel))
+            host += [table, eexp, c, np.concatenate([[0], np.cumsum(c)]).astype(np.int32),
+                     all_rows[sel].astype(np.int32), sel.astype(np.int64)]
+        d = self._stage(host)
+        for sig, j, sel in plan:
+            table, eexp, c, offs, srows, sel_d = d[j:j + 6]
+            r = D.Routing.from_plan(c, offs, srows)
+            s = _Set(*sig, table, eexp)
+            if len(plan) == 1:       # one signature (the usual case): its picks are all picks, in order
                 run_experts(s, x, row_exp, r, y, self.workspace, status, gemm_min_rows)
             else:
                 ys = torch.empty((max(len(sel), 1), H), dtype=torch.float32, device=dev)
                 run_experts(s, x, row_exp, r, ys, self.workspace, status, gemm_min_rows)
-                y[torch.from_numpy(sel).to(dev)] = ys[:len(sel)]
-        # per unique row, its picks in order: CSR for the weighted combine
-        order = np.argsort(uidx, kind="stable")
-        row_ptr = np.concatenate([[0], np.cumsum(np.bincount(uidx, minlength=len(uniq)))]).astype(np.int32)
-        dev = self.device
-        part = D.combine(y, torch.from_numpy(order.astype(np.int32)).to(dev),
-                         torch.from_numpy(all_w[order]).to(dev), len(uniq), 1,
-                         row_ptr=torch.from_numpy(row_ptr).to(dev)) if P else torch.zeros((0, H), device=dev)
+                y[sel_d] = ys[:len(sel)]
+        part = D.combine(y, d[0], d[1], len(uniq), 1, row_ptr=d[2])
         return uniq, part, status
 
 

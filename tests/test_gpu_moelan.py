@@ -134,3 +134,34 @@ def test_quant_matrix_matmul_t_for_k_quants(moelan, qtype):
         finally:
             mb.uninstall(saved)
         assert row_err(got, want) < TOL
+
+
+@pytest.mark.parametrize("fmt", ["int4", "int8", "gguf:Q4_K,Q4_K,Q6_K"])
+def test_bench_expert_runs_through_the_patched_kernels(installed, fmt):
+    """moelan's node benchmark (moelan/experts.py:342-382) with install()
+    active times this library: int4 through the patched moe_q4, int8 through
+    q8_matmul_t, GGUF K-quants through gguf_matmul_t; and moelan.accel's
+    bench_gpu is this library's (moelan/accel.py:400-411 keys)."""
+    from moelan import accel
+    from moelan.experts import bench_expert, synthetic_expert
+    import distributedmoellm_b200.kernels as K
+    calls = {"n": 0}
+    for name in ("moe_q4", "q8_matmul_t", "gguf_matmul_t"):
+        fn = getattr(installed.kernels, name)
+
+        def counted(*a, _fn=fn, **k):
+            calls["n"] += 1
+            return _fn(*a, **k)
+        setattr(installed.kernels, name, counted)
+    try:
+        ms = bench_expert(512, 256, fmt, gs=32, reps=8)
+    finally:
+        for name in ("moe_q4", "q8_matmul_t", "gguf_matmul_t"):
+            setattr(installed.kernels, name, getattr(K, name))
+    assert 0.0 < ms < 1000.0 and calls["n"] > 0
+    if fmt == "int4":
+        b = accel.bench_gpu("cuda", 1 << 28, 512, 256, "int4", 32)
+        assert set(b) == {"gpu_ms", "gpu_experts", "gpu_name"} and b["gpu_experts"] > 0
+    e = synthetic_expert(512, 256, fmt, 32)
+    x = np.random.default_rng(3).standard_normal((2, 512)).astype(np.float32)
+    assert np.isfinite(e(x)).all()
