@@ -70,6 +70,9 @@ constexpr int kMaxCachedP = 1024;  // picks whose token row and exponent the ker
 #ifndef MB_DECODE_NRED
 #define MB_DECODE_NRED 2        // reduction slots per epilogue warp with many MMA warps
 #endif
+#ifndef MB_DECODE_NRED_NARROW
+#define MB_DECODE_NRED_NARROW 1 // the same with at most 8 MMA warps (two CTAs per SM)
+#endif
 constexpr int kSegTiles = 32;   // K > 2048: row tiles of a segment whose partial sums wait in shared memory
 
 struct Fmt {
@@ -794,7 +797,7 @@ Cfg plan(int fmt, int K, int E, int RT, int P, int phase)
     if (mt0 > RT) mt0 = RT < 1 ? 1 : RT;
     // reduction buffers: with many MMA warps each epilogue warp keeps two items in
     // hand (the MMA warps run further ahead); with few, shared memory goes to stages
-    c.nred = c.KW > 8 ? MB_DECODE_NRED * kEpiWarps : kEpiWarps;
+    c.nred = (c.KW > 8 ? MB_DECODE_NRED : MB_DECODE_NRED_NARROW) * kEpiWarps;
     // one CTA per SM with many MMA warps, two with few (113 KB each leaves the per-CTA reserve)
     const size_t budget = c.KW <= 8 ? 113 * 1024 : 220 * 1024;
     const size_t cache = 2 * (size_t)(E + 1) * sizeof(int64_t) + (E <= kMaxCachedE ? (size_t)E * sizeof(void*) : 0) +
