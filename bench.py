@@ -342,14 +342,16 @@ def clone_experts(base, n):
 
 def run_gpu_ep(args, rank, world, dev):
     """Expert parallelism over the world's GPUs: rank r holds experts
-    r*E/N .. (r+1)*E/N - 1 and T tokens of its own; picked rows go to their
-    experts' ranks and back by NCCL all-to-all (distributedmoellm_b200.ep)."""
+    r*E/N .. (r+1)*E/N - 1 and T tokens of its own.  Decode: the all-gather
+    form (ep.EPGatherLayer); prefill (int8, 2048 tokens per rank): the
+    peer-memory form (ep.EPPeerLayer), rows to their experts' ranks and
+    results back by stores into the other GPUs' memory."""
     import torch
     import torch.distributed as dist
     from distributedmoellm_b200 import device as D
     from distributedmoellm_b200 import layout as L
     from distributedmoellm_b200 import synthetic as S
-    from distributedmoellm_b200.ep import DeviceOps, EPLayer
+    from distributedmoellm_b200.ep import EPPeerLayer
     from distributedmoellm_b200.store import LayerExperts
     D.require_device()
     experts, router = make_experts(0)
@@ -441,7 +443,7 @@ def run_gpu_ep(args, rank, world, dev):
             if e // El == rank:
                 q8.put_int8(e - rank * El, *parts)
         q8.publish()
-        pl = [EPLayer(DeviceOps(rt, q8, E, K_TOP), E, K_TOP, H)]
+        pl = [EPPeerLayer(rt, q8, E, K_TOP)]
         if not args.no_parity:
             def full_q8():
                 from distributedmoellm_b200.layer import MoELayer
@@ -453,9 +455,15 @@ def run_gpu_ep(args, rank, world, dev):
                 return MoELayer(rt, f8, K_TOP, True)
             parity["prefill_int8_T2048"] = ep_parity(pl[0], full_q8, 2048, rank, world, dev, 2e-3, 6000)
         for Tp in (2048,):
-            m = measure(pl, Tp, max(10, args.steps // 8), 3, 3000)
-            prefill[f"int8_T{Tp}_ep{world}"] = {"tokens_per_s": round(world * Tp / (m / 1e3), 1),
-                                               "ms_per_step": round(m, 5)}
+            m = measure(pl, Tp, max(10, args.steps // 8), 3, 3000, graphs=True)
+            prefill[f"int8_T{Tp}_ep{world}"] = {
+                "tokens_per_s": round(world * Tp / (m / 1e3), 1), "ms_per_step": round(m, 5),
+                "api": "distributedmoellm_b200.ep.EPPeerLayer (CUDA graph: counts all-gather, peer-store "
+                       "dispatch, grouped GEMMs storing results to the source ranks, combine)"}
+            if args.phases:
+                prefill[f"int8_T{Tp}_ep{world}"]["phases_us"] = ep_phase_times(
+                    pl[0], Tp, rank, dev, 20, 3, PEER_PHASES)
+        pl[0].close()
     if parity:
         prefill["parity"] = parity
     if phases:
@@ -463,14 +471,19 @@ def run_gpu_ep(args, rank, world, dev):
     return value, ms, roof, e2e, {}, None, clk.summary(), 0, prefill, None
 
 
-def ep_phase_times(layer, T, rank, dev, steps, warmup):
-    """Per-phase device time of the expert-parallel decode step (eager
-    launches, CUDA events recorded between the phases on the current stream),
-    the mean over ``steps`` steps, then the max over ranks, in microseconds."""
+GATHER_PHASES = ("route", "gather", "permute", "experts", "combine", "reduce")
+PEER_PHASES = ("route", "counts", "dispatch", "experts", "combine")
+
+
+def ep_phase_times(layer, T, rank, dev, steps, warmup, names=GATHER_PHASES):
+    """Per-phase device time of an expert-parallel step (eager launches,
+    CUDA events recorded between the phases on the current stream; a phase
+    that ends in a collective includes the wait for the slowest rank), the
+    mean over ``steps`` steps, then the max over ranks, in microseconds."""
     import torch
     import torch.distributed as dist
     x = torch.from_numpy(np.random.default_rng(77 + rank).standard_normal((T, H), dtype=np.float32)).to(dev)
-    names = ["route", "gather", "permute", "experts", "combine", "reduce"]
+    names = list(names)
     tot = {n: 0.0 for n in names}
     for it in range(warmup + steps):
         ev = {"start": torch.cuda.Event(enable_timing=True)}

@@ -48,6 +48,15 @@ SIGNATURES = {
     "mb_moe_prefill_workspace_bytes": (_i64, [_i64, _int, _int, _int]),
     "mb_moe_prefill": (_int, [_vp, _vp, _int, _int, _int, _int, _int, _int, _vp, _vp, _i64, _vp, _vp, _vp, _i64,
                               _int, _vp, _vp, _i64, _vp, _vp]),
+    "mb_peer_alloc": (_int, [_i64, ctypes.POINTER(_vp), _vp]),
+    "mb_peer_open": (_int, [_vp, ctypes.POINTER(_vp)]),
+    "mb_peer_close": (_int, [_vp]),
+    "mb_peer_free": (_int, [_vp]),
+    "mb_ep_dispatch": (_int, [_vp, _vp, _i64, _int, _vp, _vp, _int, _vp, _vp, _int, _int, _int, _vp, _vp, _vp,
+                              _i64, _vp, _vp, _vp, _vp]),
+    "mb_moe_prefill_rows_workspace_bytes": (_i64, [_i64, _int]),
+    "mb_moe_prefill_rows": (_int, [_vp, _vp, _int, _int, _int, _int, _int, _int, _vp, _vp, _vp, _vp, _i64, _int,
+                                   _vp, _vp, _vp, _int, _i64, _vp, _i64, _vp, _vp]),
     "mb_matmul_t_workspace_bytes": (_i64, [_i64]),
     "mb_matmul_t": (_int, [_vp, _int, _int, _int, _vp, _i64, _vp, _vp, _i64, _vp, _vp]),
 }

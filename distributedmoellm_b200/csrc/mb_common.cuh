@@ -64,6 +64,34 @@ int mb_num_sms();
 #define MB_STATUS_TIMEOUT 1u
 #define MB_STATUS_BADARG 2u
 
+// ---- f16 token rows ---------------------------------------------------------------
+// The grouped GEMM reads its tokens as f16 rows, each scaled by 2^row_exp and
+// stored in the K order 0 4 1 5 2 6 3 7 within every 8 columns (the order its
+// tensor-core operand tiles expect); the token gather and the expert-parallel
+// dispatch both write them with these helpers.
+
+__device__ __forceinline__ uint32_t pack_f16(float lo, float hi)
+{
+    const __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// 2^e for -126 <= e <= 127, exact.
+__device__ __forceinline__ float pow2i(int e) { return __int_as_float((e + 127) << 23); }
+
+__device__ __forceinline__ int clamp120(int e) { return e < -120 ? -120 : (e > 120 ? 120 : e); }
+
+// Eight f32 values as four f16 pairs in the K order 0 4 1 5 2 6 3 7.
+__device__ __forceinline__ uint4 pack8_perm(const float4 lo, const float4 hi, float sc)
+{
+    uint4 o;
+    o.x = pack_f16(lo.x * sc, hi.x * sc);
+    o.y = pack_f16(lo.y * sc, hi.y * sc);
+    o.z = pack_f16(lo.z * sc, hi.z * sc);
+    o.w = pack_f16(lo.w * sc, hi.w * sc);
+    return o;
+}
+
 // Upper bound for one bounded wait, in nanoseconds of %globaltimer.
 #define MB_WAIT_LIMIT_NS 2000000000ull
 

@@ -87,12 +87,19 @@ struct PrefillArgs {
     int block_bytes;
     const int32_t* counts;
     const int32_t* offsets;
-    const int32_t* sorted_rows;
+    const int32_t* sorted_rows;   // the token row of each pick, or null: pick p is row p
     const int32_t* row_exp;    // exponents of the rows of x
     int min_rows;
     int O_real;                // phase 1: I (act columns); phase 2: H (y columns)
     __half* act;               // phase 1 output (P, I), K-permuted
     float* y;                  // phase 2 output (P, H)
+    // phase 2 output rows elsewhere (expert parallelism): pick p's row goes to
+    // y_peers[y_ret[p] >> 24] + (y_ret[p] & 0xffffff) * H instead of y + p * H
+    // (an address outside n_peers buffers of peer_rows rows is reported and skipped)
+    const int32_t* y_ret;
+    float* const* y_peers;
+    int n_peers;
+    int64_t peer_rows;
     unsigned* status;
     // precise gate|up (affine int4): the weights' f16 rounding (piece 0) or its f16 residual (piece 1), and
     // the gate and up pre-activations written (accumulate 0) or added (1) to pre (P, 2I) f32 instead of act
@@ -190,17 +197,6 @@ __device__ __forceinline__ uint32_t idesc_f16(int n)
     return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
 }
 
-__device__ __forceinline__ uint32_t pack_f16(float lo, float hi)
-{
-    const __half2 v = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<const uint32_t*>(&v);
-}
-
-// 2^e for -126 <= e <= 127, exact.
-__device__ __forceinline__ float pow2i(int e) { return __int_as_float((e + 127) << 23); }
-
-__device__ __forceinline__ int clamp120(int e) { return e < -120 ? -120 : (e > 120 ? 120 : e); }
-
 // The static sequence of work items every role of a CTA walks: items
 // blockIdx.x, blockIdx.x + gridDim.x, ... of E * MB, skipping experts
 // outside this launch.
@@ -280,7 +276,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* pst = bst + kBStages * 2 * kBHalf;                // [kPStages][8 tiles][block]
     float* tok_s = reinterpret_cast<float*>(pst + kPStages * 8 * a.block_bytes);   // [2][kMaxN] row scale
     float* tok_a = tok_s + 2 * kMaxN;                          // [2][kMaxN] activation scale (phase 1)
-    uint64_t* bars = reinterpret_cast<uint64_t*>(tok_a + 2 * kMaxN);
+    float** tok_y = reinterpret_cast<float**>(tok_a + 2 * kMaxN);   // [2][kMaxN] output row (phase 2)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(tok_y + 2 * kMaxN);
     uint64_t* b_full = bars;                                   // [kBStages]
     uint64_t* b_empty = b_full + kBStages;
     uint64_t* p_full = b_empty + kBStages;                     // [kPStages]
@@ -571,13 +568,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int npad = (nrows + 15) & ~15;
                 float* ts = tok_s + slot * kMaxN;
                 float* ta = tok_a + slot * kMaxN;
+                float** ty = tok_y + slot * kMaxN;
                 for (int n = et; n < ((nrows + 31) & ~31); n += 128) {   // padding tokens: scale 0
                     float s0 = 0.f, s1 = 0.f;
                     if (n < nrows) {
-                        const int rexp = a.row_exp[a.sorted_rows[w.off_e + n0 + n]];
+                        const int pick = w.off_e + n0 + n;
+                        const int rexp = a.row_exp[a.sorted_rows ? a.sorted_rows[pick] : pick];
                         const int ea = clamp120(w.aexp + 2 * rexp);
                         s0 = pow2i(a.phase == 1 ? -clamp120(rexp) : -ea);
                         s1 = pow2i(ea);
+                        if (a.phase == 2) {
+                            if (a.y_ret) {
+                                const uint32_t r = (uint32_t)a.y_ret[pick];
+                                const int src = (int)(r >> 24);
+                                const int64_t row = (int64_t)(r & 0xffffffu);
+                                if (src < a.n_peers && row < a.peer_rows) {
+                                    ty[n] = a.y_peers[src] + row * a.O_real;
+                                } else {
+                                    ty[n] = nullptr;
+                                    atomicOr(a.status, MB_STATUS_BADARG);
+                                }
+                            } else {
+                                ty[n] = a.y + (int64_t)pick * a.O_real;
+                            }
+                        }
                     }
                     ts[n] = s0;
                     ta[n] = s1;
@@ -629,12 +643,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     } else {
                         const int o = w.mb * kBM + L;
+                        float* const* ty = tok_y + slot * kMaxN;
 #pragma unroll
                         for (int i = 0; i < 32; ++i) {
                             const int n = cb + i;
-                            if (n < nrows && o < a.O_real)
-                                a.y[(int64_t)(w.off_e + n0 + n) * a.O_real + o] =
-                                    __uint_as_float(r[i]) * ts[n] * wunscale;
+                            if (n < nrows && o < a.O_real && ty[n]) ty[n][o] = __uint_as_float(r[i]) * ts[n] * wunscale;
                         }
                     }
                 }
@@ -643,23 +656,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) mb_mbar_arrive(&acc_empty[slot]);
             }
         }
+        if (a.y_ret) __threadfence_system();   // rows stored to other GPUs are seen before what follows the launch
     }
 
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     if (warp == 2) tmem_dealloc(tmem, kTmemCols);
-}
-
-// Eight f32 values as four f16 pairs in the K order 0 4 1 5 2 6 3 7.
-__device__ __forceinline__ uint4 pack8_perm(const float4 lo, const float4 hi, float sc)
-{
-    uint4 o;
-    o.x = pack_f16(lo.x * sc, hi.x * sc);
-    o.y = pack_f16(lo.y * sc, hi.y * sc);
-    o.z = pack_f16(lo.z * sc, hi.z * sc);
-    o.w = pack_f16(lo.w * sc, hi.w * sc);
-    return o;
 }
 
 // The picks' tokens in pick order as f16, each row scaled by 2^row_exp[row]
@@ -773,7 +776,7 @@ int block_bytes_of(int fmt)
 size_t smem_bytes(int fmt, int block_bytes, int E)
 {
     const int ps = pstages(fmt == MB_FMT_Q8_F16 || fmt == MB_FMT_Q8_F32);
-    return 1024 + (size_t)kBStages * 2 * kBHalf + (size_t)ps * 8 * block_bytes + 4 * kMaxN * 4 +
+    return 1024 + (size_t)kBStages * 2 * kBHalf + (size_t)ps * 8 * block_bytes + 4 * kMaxN * 4 + 2 * kMaxN * 8 +
            (2 * kBStages + 2 * ps + 2 * kASlots + 4) * 8 + 16 + (size_t)E * 16;
 }
 
@@ -812,6 +815,61 @@ int dispatch(int fmt, const PrefillArgs& a, const TokenMaps& map, cudaStream_t s
 }
 
 int64_t r1k(int64_t n) { return (n + 1023) / 1024 * 1024; }
+
+// The GEMM launches of one layer over tokens already in f16 rows xp (P x H, pick order, K-permuted, each
+// scaled by 2^row_exp): gate|up into a.act (with the precise three-product form when fmt_gu is
+// MB_FMT_Q4K_F32: xp_lo the residual rows, pre the f32 pre-activations), then down into the output rows.
+int run_gemms(PrefillArgs a, int H, int I, int fmt_gu, int fmt_down, const __half* xp, const __half* xp_lo,
+              float* pre, int64_t P, cudaStream_t st)
+{
+    TokenMaps map;
+    // gate|up: K = H, rows 2I (RT = I/8 tiles of 8 gate + 8 up rows) -> act (P, I) f16
+    int rc = f16_maps(&map, xp, P, H);
+    if (rc) return rc;
+    a.phase = 1;
+    a.NQ = H / 128;
+    a.KH = H / 64;
+    a.RT = I / 8;
+    a.MB = (a.RT + 7) / 8;
+    a.block_bytes = block_bytes_of(fmt_gu);
+    a.O_real = I;
+    if (fmt_gu != MB_FMT_Q4K_F32) {
+        rc = dispatch(fmt_gu, a, map, st);
+        if (rc) return rc;
+    } else {
+        // three products with f16 operands, each exact in its f32 accumulation: W_hi x_hi + W_hi x_lo + W_lo x_hi
+        // (W_lo x_lo is below f32 rounding of the sum), then SiLU(gate) * up from the f32 sums
+        TokenMaps map_lo;
+        rc = f16_maps(&map_lo, xp_lo, P, H);
+        if (rc) return rc;
+        a.pre = pre;
+        const TokenMaps* maps[3] = {&map, &map_lo, &map};
+        for (int pass = 0; pass < 3; ++pass) {
+            a.piece = pass == 2 ? 1 : 0;
+            a.accumulate = pass > 0;
+            rc = dispatch(fmt_gu, a, *maps[pass], st);
+            if (rc) return rc;
+        }
+        a.pre = nullptr;
+        a.piece = a.accumulate = 0;
+        swiglu_act_kernel<<<(unsigned)((P + 7) / 8), 256, 0, st>>>(pre, P, I, a.offsets, a.E, a.e_exp,
+                                                                   a.sorted_rows, a.row_exp, a.act);
+        rc = mb_check_launch("mb_moe_prefill swiglu");
+        if (rc) return rc;
+    }
+
+    // down: K = I, rows H -> y (P, H)
+    rc = f16_maps(&map, a.act, P, I);
+    if (rc) return rc;
+    a.phase = 2;
+    a.NQ = (I + 127) / 128;
+    a.KH = I / 64;
+    a.RT = H / 16;
+    a.MB = (a.RT + 7) / 8;
+    a.block_bytes = block_bytes_of(fmt_down);
+    a.O_real = H;
+    return dispatch(fmt_down, a, map, st);
+}
 
 }  // namespace
 
@@ -875,52 +933,59 @@ extern "C" int mb_moe_prefill(const MbExpert* table, const int32_t* e_exp, int E
     a.status = status;
     a.act = act;
     a.y = y;
+    return run_gemms(a, H, I, fmt_gu, fmt_down, xp, xp_lo, pre, P, st);
+}
 
-    TokenMaps map;
-    // gate|up: K = H, rows 2I (RT = I/8 tiles of 8 gate + 8 up rows) -> act (P, I) f16
-    rc = f16_maps(&map, xp, P, H);
-    if (rc) return rc;
-    a.phase = 1;
-    a.NQ = H / 128;
-    a.KH = H / 64;
-    a.RT = I / 8;
-    a.MB = (a.RT + 7) / 8;
-    a.block_bytes = block_bytes_of(fmt_gu);
-    a.O_real = I;
-    if (!precise) {
-        rc = dispatch(fmt_gu, a, map, st);
-        if (rc) return rc;
-    } else {
-        // three products with f16 operands, each exact in its f32 accumulation: W_hi x_hi + W_hi x_lo + W_lo x_hi
-        // (W_lo x_lo is below f32 rounding of the sum), then SiLU(gate) * up from the f32 sums
-        TokenMaps map_lo;
-        rc = f16_maps(&map_lo, xp_lo, P, H);
-        if (rc) return rc;
-        a.pre = pre;
-        const TokenMaps* maps[3] = {&map, &map_lo, &map};
-        for (int pass = 0; pass < 3; ++pass) {
-            a.piece = pass == 2 ? 1 : 0;
-            a.accumulate = pass > 0;
-            rc = dispatch(fmt_gu, a, *maps[pass], st);
-            if (rc) return rc;
-        }
-        a.pre = nullptr;
-        a.piece = a.accumulate = 0;
-        swiglu_act_kernel<<<(unsigned)((P + 7) / 8), 256, 0, st>>>(pre, P, I, offsets, E, e_exp, sorted_rows,
-                                                                   row_exp, act);
-        rc = mb_check_launch("mb_moe_prefill swiglu");
-        if (rc) return rc;
+// Workspace (from its first 1024-byte boundary): the activations as f16 (P x I) | status word.
+extern "C" int64_t mb_moe_prefill_rows_workspace_bytes(int64_t P, int I)
+{
+    return 1024 + r1k(P * I * 2) + 256;
+}
+
+extern "C" int mb_moe_prefill_rows(const MbExpert* table, const int32_t* e_exp, int E, int H, int I, int gs,
+                                   int fmt_gu, int fmt_down, const void* xp, const int32_t* row_exp,
+                                   const int32_t* counts, const int32_t* offsets, int64_t P, int min_rows, float* y,
+                                   const int32_t* y_ret, float* const* y_peers, int n_peers, int64_t peer_rows,
+                                   void* workspace, int64_t workspace_bytes, unsigned* status, void* stream)
+{
+    MB_REQUIRE(table && e_exp && xp && row_exp && counts && offsets && workspace && (y || (y_ret && y_peers)),
+               "mb_moe_prefill_rows: null pointer");
+    MB_REQUIRE(!y_ret || (n_peers >= 1 && n_peers <= 256 && peer_rows >= 0),
+               "mb_moe_prefill_rows: %d result buffers of %lld rows", n_peers, (long long)peer_rows);
+    MB_REQUIRE(E > 0 && E <= kMaxMetaE && P >= 0 && P < (1ll << 24),
+               "mb_moe_prefill_rows: E=%d (at most %d experts), P=%lld (below 2^24)", E, kMaxMetaE, (long long)P);
+    MB_REQUIRE(H % 128 == 0 && I % 64 == 0 && H > 0 && I > 0,
+               "mb_moe_prefill_rows: needs H %% 128 == 0 and I %% 64 == 0 (H=%d I=%d)", H, I);
+    MB_REQUIRE(gs % 32 == 0 && H % gs == 0 && I % gs == 0, "mb_moe_prefill_rows: group size %d", gs);
+    MB_REQUIRE(((uintptr_t)xp & 15) == 0 && ((uintptr_t)workspace & 15) == 0,
+               "mb_moe_prefill_rows: xp and workspace must be 16-byte aligned");
+    MB_REQUIRE(workspace_bytes >= mb_moe_prefill_rows_workspace_bytes(P, I), "mb_moe_prefill_rows: workspace too small");
+    if (fmt_gu == MB_FMT_Q4K_F32)
+        return mb_fail(MB_EUNSUPPORTED, "mb_moe_prefill_rows: the precise Q4_K gate|up needs the tokens' f32 rows");
+    if (P == 0) return MB_OK;
+    cudaStream_t st = mb_stream(stream);
+    uint8_t* ws = reinterpret_cast<uint8_t*>(((uintptr_t)workspace + 1023) & ~(uintptr_t)1023);
+    __half* act = reinterpret_cast<__half*>(ws);
+    ws += r1k(P * I * 2);
+    if (!status) {
+        status = reinterpret_cast<unsigned*>(ws);
+        cudaMemsetAsync(status, 0, sizeof(unsigned), st);
     }
-
-    // down: K = I, rows H -> y (P, H)
-    rc = f16_maps(&map, act, P, I);
-    if (rc) return rc;
-    a.phase = 2;
-    a.NQ = (I + 127) / 128;
-    a.KH = I / 64;
-    a.RT = H / 16;
-    a.MB = (a.RT + 7) / 8;
-    a.block_bytes = block_bytes_of(fmt_down);
-    a.O_real = H;
-    return dispatch(fmt_down, a, map, st);
+    PrefillArgs a{};
+    a.table = table;
+    a.e_exp = e_exp;
+    a.E = E;
+    a.counts = counts;
+    a.offsets = offsets;
+    a.sorted_rows = nullptr;
+    a.row_exp = row_exp;
+    a.min_rows = min_rows < 1 ? 1 : min_rows;
+    a.status = status;
+    a.act = act;
+    a.y = y;
+    a.y_ret = y_ret;
+    a.y_peers = y_peers;
+    a.n_peers = n_peers;
+    a.peer_rows = peer_rows;
+    return run_gemms(a, H, I, fmt_gu, fmt_down, reinterpret_cast<const __half*>(xp), nullptr, nullptr, P, st);
 }

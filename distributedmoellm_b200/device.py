@@ -330,3 +330,72 @@ def matmul_t(w_tiles: torch.Tensor, fmt: int, O: int, K: int, x: torch.Tensor, y
 
 
 __all__ = [n for n in dir() if not n.startswith("_")] + ["_lib"]
+
+
+# ---- expert parallelism through peer memory ---------------------------------------------
+
+PEER_HANDLE_BYTES = 64
+
+
+def peer_alloc(nbytes: int) -> tuple[int, bytes]:
+    """nbytes of device memory on the current device that other processes of
+    the node can map: (address, handle for peer_open)."""
+    ptr = ctypes.c_void_p()
+    h = ctypes.create_string_buffer(PEER_HANDLE_BYTES)
+    check(lib().mb_peer_alloc(int(nbytes), ctypes.byref(ptr), h), "mb_peer_alloc")
+    return int(ptr.value), h.raw
+
+
+def peer_open(handle: bytes) -> int:
+    """This process's address of another process's peer_alloc memory."""
+    if len(handle) != PEER_HANDLE_BYTES:
+        raise ValueError(f"a peer handle has {PEER_HANDLE_BYTES} bytes, got {len(handle)}")
+    ptr = ctypes.c_void_p()
+    check(lib().mb_peer_open(ctypes.c_char_p(bytes(handle)), ctypes.byref(ptr)), "mb_peer_open")
+    return int(ptr.value)
+
+
+def peer_close(ptr: int) -> None:
+    check(lib().mb_peer_close(ctypes.c_void_p(ptr)), "mb_peer_close")
+
+
+def peer_free(ptr: int) -> None:
+    check(lib().mb_peer_free(ctypes.c_void_p(ptr)), "mb_peer_free")
+
+
+def ep_dispatch(x: torch.Tensor, row_exp: torch.Tensor, idx: torch.Tensor, r: Routing, counts_all: torch.Tensor,
+                rank: int, recv_rows: torch.Tensor, recv_exp: torch.Tensor, recv_ret: torch.Tensor, cap: int,
+                local_counts: torch.Tensor, local_offsets: torch.Tensor, status: torch.Tensor):
+    """This rank's picks (idx (T, k), permuted into ``r``) stored into their
+    experts' ranks' receive rows; recv_*: int64 device tensors of G
+    addresses; counts_all (G, E) every rank's counts."""
+    _cuda(x, row_exp, idx, counts_all, recv_rows, recv_exp, recv_ret, local_counts, local_offsets, status)
+    T, k = idx.shape
+    G, E = counts_all.shape
+    check(lib().mb_ep_dispatch(_p(x), _p(row_exp), T, x.shape[1], _p(idx), _p(r.inv), k, _p(r.offsets),
+                               _p(counts_all), E, G, int(rank), _p(recv_rows), _p(recv_exp), _p(recv_ret), int(cap),
+                               _p(local_counts), _p(local_offsets), _p(status), _stream()), "mb_ep_dispatch")
+
+
+def prefill_rows_workspace_bytes(P: int, I: int) -> int:
+    return int(lib().mb_moe_prefill_rows_workspace_bytes(P, I))
+
+
+def moe_prefill_rows(experts, xp: int, row_exp: int, counts: torch.Tensor, offsets: torch.Tensor, P: int,
+                     workspace: torch.Tensor, y: torch.Tensor | None = None, y_ret: int | None = None,
+                     y_peers: torch.Tensor | None = None, peer_rows: int = 0, status: torch.Tensor | None = None,
+                     min_rows: int = 1):
+    """The grouped GEMMs of ``experts`` (a LayerExperts) over P f16 operand
+    rows at address ``xp`` (exponents at ``row_exp``), grouped by counts /
+    offsets; output rows into y, or to the return addresses at ``y_ret``
+    over the row buffers (``peer_rows`` rows each) listed in ``y_peers``
+    (int64 device tensor)."""
+    ex = experts
+    _cuda(counts, offsets, workspace, y, y_peers, status)
+    n_peers = 0 if y_peers is None else y_peers.numel()
+    check(lib().mb_moe_prefill_rows(_p(ex.table), _p(ex.eexp), ex.E, ex.H, ex.I, ex.gs, ex.fmt_gu, ex.fmt_down,
+                                    ctypes.c_void_p(xp), ctypes.c_void_p(row_exp), _p(counts), _p(offsets), int(P),
+                                    int(min_rows), _p(y), None if y_ret is None else ctypes.c_void_p(y_ret),
+                                    _p(y_peers), n_peers, int(peer_rows), _p(workspace),
+                                    workspace.numel() * workspace.element_size(), _p(status), _stream()),
+          "mb_moe_prefill_rows")

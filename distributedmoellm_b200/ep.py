@@ -40,6 +40,7 @@ import torch
 import torch.distributed as dist
 
 from . import device as D
+from .layout import FMT_Q4K_F32
 from .layer import GEMM_MIN_ROWS, run_experts
 
 
@@ -167,6 +168,19 @@ class DeviceOps:
         return D.combine(y, inv, w, T, k, out=out)
 
 
+def _capture(forward, x: torch.Tensor) -> torch.cuda.CUDAGraph:
+    """A CUDA graph of forward(x) after one warm-up call on a side stream."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        forward(x)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        forward(x)
+    return g
+
+
 class _GatherBuffers:
     def __init__(self, T, world, E, k, H, I, dev):
         TA, P = T * world, T * world * k
@@ -262,15 +276,163 @@ class EPGatherLayer:
         """A CUDA graph of forward(x), collectives included, on x's current
         contents; replay it after writing new inputs into x.  Output:
         buffers(T).out.  Release the graph before destroying the process group."""
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            self.forward(x)
-        torch.cuda.current_stream().wait_stream(s)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            self.forward(x)
-        return g
+        return _capture(self.forward, x)
 
     def status(self, T: int) -> int:
         return int(self.buffers(T).status.item())
+
+
+class _DeviceView:
+    """A device address as a torch tensor (CUDA array interface, no copy)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "strides": None, "version": 3}
+
+
+def _r1k(n: int) -> int:
+    return (n + 1023) // 1024 * 1024
+
+
+class _PeerBuffers:
+    """EPPeerLayer's buffers for batches of T tokens on one rank.  The arena
+    (mapped by every rank) holds: receive rows (cap, H) f16 | their exponents
+    (cap,) | their return addresses (cap,) | the result rows of this rank's
+    own picks (T*k, H) f32; cap = G*T*k, the most any rank can receive."""
+
+    def __init__(self, T, world, rank, E, k, H, I, dev, group):
+        P = T * k
+        self.T, self.P = T, P
+        self.cap = cap = world * P
+        self.off_exp = _r1k(cap * H * 2)
+        self.off_ret = self.off_exp + _r1k(cap * 4)
+        self.off_y = self.off_ret + _r1k(cap * 4)
+        nbytes = self.off_y + _r1k(max(P, 1) * H * 4)
+        self.opened: list[int] = []
+        self.base, handle = D.peer_alloc(nbytes)
+        try:
+            mine = torch.tensor(list(handle), dtype=torch.uint8, device=dev)
+            every = torch.empty((world, D.PEER_HANDLE_BYTES), dtype=torch.uint8, device=dev)
+            dist.all_gather_into_tensor(every, mine, group=group)
+            every = every.cpu().numpy()
+            bases = []
+            for s in range(world):
+                if s == rank:
+                    bases.append(self.base)
+                else:
+                    self.opened.append(D.peer_open(every[s].tobytes()))
+                    bases.append(self.opened[-1])
+        except BaseException:
+            self.close()
+            raise
+
+        def table(off):
+            return torch.tensor([b + off for b in bases], dtype=torch.int64, device=dev)
+        self.peer_rows, self.peer_exp, self.peer_ret, self.peer_y = (table(0), table(self.off_exp),
+                                                                     table(self.off_ret), table(self.off_y))
+        self.y_home = torch.as_tensor(_DeviceView(self.base + self.off_y, (max(P, 1), H), "<f4"), device=dev)
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.row_exp = torch.empty(T, **i32)
+        self.idx = torch.empty((T, k), **i32)
+        self.w = torch.empty((T, k), dtype=torch.float32, device=dev)
+        self.routing = D.Routing(T, k, E, dev)
+        self.rws = torch.empty(D.router_workspace_bytes(T, H, E), dtype=torch.uint8, device=dev)
+        self.counts_all = torch.zeros((world, E), **i32)
+        El = E // world
+        self.local_counts = torch.zeros(El, **i32)
+        self.local_offsets = torch.zeros(El + 1, **i32)
+        self.ws = torch.empty(D.prefill_rows_workspace_bytes(cap, I), dtype=torch.uint8, device=dev)
+        self.status = torch.zeros(1, **i32)
+        self.flag = torch.zeros(1, **i32)
+        self.ident = torch.arange(max(P, 1), **i32)
+        self.out = torch.empty((T, H), dtype=torch.float32, device=dev)
+
+    def close(self):
+        for p in self.opened:
+            D.peer_close(p)
+        self.opened = []
+
+    def free(self):
+        if self.base:
+            D.peer_free(self.base)
+            self.base = 0
+
+
+class EPPeerLayer:
+    """One MoE layer over the ranks of ``group`` for prefill-sized batches,
+    with no host round trip: every rank routes its own tokens, an all-gather
+    of the per-expert pick counts (E integers per rank) fixes where every
+    rank's rows land, mb_ep_dispatch stores each pick's token row into its
+    expert's rank's receive rows (as the grouped GEMM's f16 operand), the
+    rank's grouped GEMMs run over what it received and their epilogue stores
+    each result row back into the source rank's result rows, and each rank
+    combines its own picks.  Two one-integer all-reduces order the ranks
+    (rows complete before the GEMMs read them; results complete before the
+    combine).  ``experts``: this rank's E/G local experts as local ids
+    0 .. E/G-1.  Every rank calls forward (and buffers) with the same T in
+    the same order; close() on every rank releases the peer memory."""
+
+    def __init__(self, router: torch.Tensor, experts, E: int, top_k: int, normalize: bool = True, group=None):
+        self.router = router.contiguous()
+        self.experts, self.E, self.k, self.normalize, self.group = experts, E, top_k, normalize, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if E % self.world or experts.E != E // self.world:
+            raise ValueError(f"E={E} experts do not split into {self.world} slices of {experts.E}")
+        if experts.fmt_gu == FMT_Q4K_F32:
+            raise ValueError("EPPeerLayer: Q4_K experts need the precise gate|up form over f32 rows; use EPLayer")
+        self.E_local = E // self.world
+        self._bufs: dict = {}
+
+    def buffers(self, T: int) -> _PeerBuffers:
+        b = self._bufs.get(T)
+        if b is None:
+            ex = self.experts
+            b = self._bufs[T] = _PeerBuffers(T, self.world, self.rank, self.E, self.k, ex.H, ex.I,
+                                             self.router.device, self.group)
+        return b
+
+    def forward(self, x: torch.Tensor, mark=None) -> torch.Tensor:
+        """``mark(name)``, when given, is called after each phase (route,
+        counts, dispatch, experts, combine) as its work is enqueued."""
+        mark = mark or (lambda name: None)
+        T = x.shape[0]
+        b = self.buffers(T)
+        x = x.contiguous()
+        D.router_route(x, self.router, self.k, self.normalize, b.idx, b.w, row_exp=b.row_exp, workspace=b.rws)
+        r = D.permute(b.idx, b.w, self.E, b.routing)
+        mark("route")
+        dist.all_gather_into_tensor(b.counts_all, r.counts, group=self.group)
+        mark("counts")
+        D.ep_dispatch(x, b.row_exp, b.idx, r, b.counts_all, self.rank, b.peer_rows, b.peer_exp, b.peer_ret, b.cap,
+                      b.local_counts, b.local_offsets, b.status)
+        dist.all_reduce(b.flag, op=dist.ReduceOp.MAX, group=self.group)     # every rank's rows have landed
+        mark("dispatch")
+        D.moe_prefill_rows(self.experts, b.base, b.base + b.off_exp, b.local_counts, b.local_offsets, b.cap, b.ws,
+                           y_ret=b.base + b.off_ret, y_peers=b.peer_y, peer_rows=b.P, status=b.status)
+        dist.all_reduce(b.flag, op=dist.ReduceOp.MAX, group=self.group)     # every result row has landed
+        mark("experts")
+        D.combine(b.y_home, b.ident[:b.P], b.w.view(-1), T, self.k, out=b.out)
+        mark("combine")
+        return b.out
+
+    __call__ = forward
+
+    def capture(self, x: torch.Tensor) -> torch.cuda.CUDAGraph:
+        """A CUDA graph of forward(x), collectives included (see
+        EPGatherLayer.capture)."""
+        return _capture(self.forward, x)
+
+    def status(self, T: int) -> int:
+        return int(self.buffers(T).status.item())
+
+    def close(self) -> None:
+        """Unmap the other ranks' arenas, wait for every rank to do the same,
+        then free this rank's own (collective: every rank calls it)."""
+        torch.cuda.synchronize()
+        for b in self._bufs.values():
+            b.close()
+        dist.barrier(group=self.group)
+        for b in self._bufs.values():
+            b.free()
+        self._bufs = {}

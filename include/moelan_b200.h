@@ -282,6 +282,67 @@ int mb_moe_prefill(const MbExpert *table, const int32_t *e_exp, int E, int H, in
                    const int32_t *offsets, const int32_t *sorted_rows, int64_t P, int min_rows, float *y,
                    void *workspace, int64_t workspace_bytes, unsigned *status, void *stream);
 
+/* ---- expert parallelism over the GPUs of one node (peer memory) ----------
+ *
+ * The reference's coordinator sends each worker one request per layer with
+ * the rows routed to its experts and adds the results back
+ * (moelan/coordinator.py:475-535); across the GPUs of one node (one process
+ * per GPU) the rows move by stores into the other GPUs' memory instead.
+ * Each rank allocates one arena with mb_peer_alloc, the ranks exchange the
+ * handles (any host channel), and each maps the others' arenas with
+ * mb_peer_open.  Ranks must not use an arena after its owner freed it. */
+#define MB_PEER_HANDLE_BYTES 64
+
+/* bytes of device memory, plus the handle (MB_PEER_HANDLE_BYTES) another
+ * process of the node passes to mb_peer_open. */
+int mb_peer_alloc(int64_t bytes, void **ptr, void *handle);
+int mb_peer_open(const void *handle, void **ptr);
+int mb_peer_close(void *ptr);   /* a mapping made by mb_peer_open */
+int mb_peer_free(void *ptr);    /* an arena made by mb_peer_alloc */
+
+/* One rank's dispatch of its own tokens to their experts' ranks (E experts,
+ * expert e on rank e / (E/G)).  Inputs: x (T, H) f32 and row_exp (T,) (from
+ * mb_router_route / mb_row_exponents), the picks idx (T, k) and, from
+ * mb_permute of them, inv (T*k,) and offsets (E+1,); counts_all (G, E): every
+ * rank's per-expert pick counts (row s = rank s's mb_permute counts).  The
+ * receive rows of rank d are grouped by d's local expert, within an expert by
+ * source rank, within a source in its mb_permute order; pick p of this rank
+ * is stored there as the grouped GEMM's f16 operand row (scaled by
+ * 2^row_exp, K order as mb_moe_prefill_rows reads it), with its exponent in
+ * recv_exp and its return address (rank << 24 | p) in recv_ret.  recv_rows,
+ * recv_exp, recv_ret: device arrays of G pointers (each rank's (cap, H) f16,
+ * (cap,) and (cap,) int32, as mapped in this process).  Also writes this
+ * rank's own receive plan: local_counts (E/G,) and local_offsets (E/G + 1,).
+ * A pick that would land at or past cap sets MB_STATUS_BADARG in *status and
+ * is skipped; cap = G*T*k always suffices.  Needs T*k < 2^24, H % 128 == 0.
+ * The stores into other ranks' memory are complete when the launch is: a
+ * stream-ordered collective after it (or any barrier that orders the ranks)
+ * makes the rows safe to read on their ranks. */
+int mb_ep_dispatch(const float *x, const int32_t *row_exp, int64_t T, int H, const int32_t *idx,
+                   const int32_t *inv, int k, const int32_t *offsets, const int32_t *counts_all, int E, int G,
+                   int rank, void *const *recv_rows, int32_t *const *recv_exp, int32_t *const *recv_ret,
+                   int64_t cap, int32_t *local_counts, int32_t *local_offsets, unsigned *status, void *stream);
+
+/* Workspace bytes for mb_moe_prefill_rows with P rows. */
+int64_t mb_moe_prefill_rows_workspace_bytes(int64_t P, int I);
+
+/* mb_moe_prefill over tokens already in the GEMM's f16 operand rows: xp
+ * (P, H) as mb_ep_dispatch writes them, row_exp (P,) their exponents,
+ * counts / offsets (E / E+1) the rows of each expert (rows past offsets[E]
+ * are not read).  Output row p goes to y + p*H, or, when y_ret and y_peers
+ * are given, to y_peers[y_ret[p] >> 24] + (y_ret[p] & 0xffffff) * H
+ * (y_peers: a device array of n_peers row-buffer pointers, e.g. every rank's
+ * result rows as mapped in this process, each of peer_rows rows), stored from
+ * the GEMM epilogue; an address outside those buffers sets MB_STATUS_BADARG
+ * in *status and its row is not stored.  Not for
+ * fmt_gu MB_FMT_Q4K_F32 (MB_EUNSUPPORTED: its precise form needs the f32
+ * rows).  P < 2^24. */
+int mb_moe_prefill_rows(const MbExpert *table, const int32_t *e_exp, int E, int H, int I, int gs, int fmt_gu,
+                        int fmt_down, const void *xp, const int32_t *row_exp, const int32_t *counts,
+                        const int32_t *offsets, int64_t P, int min_rows, float *y, const int32_t *y_ret,
+                        float *const *y_peers, int n_peers, int64_t peer_rows, void *workspace,
+                        int64_t workspace_bytes, unsigned *status, void *stream);
+
 /* Workspace bytes for mb_matmul_t with n input rows. */
 int64_t mb_matmul_t_workspace_bytes(int64_t n);
 

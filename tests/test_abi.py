@@ -48,8 +48,21 @@ def test_bad_arguments_are_rejected_on_the_host(L):
     assert L.mb_permute(p, p, 70000, 1, 8, p, p, p, p, p, p, p, p, None) == 1
     assert L.mb_moe_decode(p, 8, 256, 512, 16, 2, 2, p, p, 1, p, p, p, 2, 0, p, p, 1 << 20, None, None) == 1
     assert "group size" in _lib.last_error()
+    # expert-parallel dispatch and the pre-gathered GEMM: shapes checked before any device work
+    assert L.mb_ep_dispatch(p, p, 4, 256, p, p, 2, p, p, 8, 3, 0, p, p, p, 64, p, p, p, None) == 1   # 8 % 3
+    assert L.mb_ep_dispatch(p, p, 4, 200, p, p, 2, p, p, 8, 2, 0, p, p, p, 64, p, p, p, None) == 1   # H % 128
+    assert L.mb_ep_dispatch(p, p, 4, 256, p, p, 2, p, p, 8, 2, 2, p, p, p, 64, p, p, p, None) == 1   # rank
+    assert L.mb_ep_dispatch(p, p, 1 << 23, 256, p, p, 2, p, p, 8, 2, 0, p, p, p, 64, p, p, p, None) == 1
+    assert L.mb_moe_prefill_rows(p, p, 8, 256, 256, 32, 2, 2, p, p, p, p, 1 << 24, 1, p, None, None, 0, 0, p,
+                                 1 << 30, None, None) == 1
+    assert L.mb_moe_prefill_rows(p, p, 8, 256, 256, 32, 2, 2, p, p, p, p, 64, 1, None, p, p, 0, 64, p,
+                                 1 << 30, None, None) == 1                                   # no result buffers
+    assert L.mb_moe_prefill_rows(p, p, 8, 256, 256, 32, 5, 2, p, p, p, p, 64, 1, p, None, None, 0, 0, p,
+                                 1 << 30, None, None) == 3                                   # Q4_K gate|up
+    assert L.mb_peer_open(None, None) == 1
 
 
 def test_workspace_sizes(L):
     assert L.mb_moe_decode_workspace_bytes(512, 768) >= 512 * 768 * 4 + 512 * 4
     assert L.mb_matmul_t_workspace_bytes(17) >= 17 * 4
+    assert L.mb_moe_prefill_rows_workspace_bytes(4096, 768) >= 4096 * 768 * 2

@@ -153,6 +153,45 @@ def test_local_plan_regroups_by_local_expert():
         assert got == want
 
 
+def test_oracle_receive_plan_is_the_local_plan_grouping():
+    """The peer-memory dispatch's receive order (the oracle's
+    ep_receive_plan: by local expert, then source rank, then the source's
+    grouping order) is the order local_plan gives the all-to-all's receive
+    buffer (source-major) once regrouped."""
+    sys.path.insert(0, str(ROOT))
+    import oracle as O
+    from distributedmoellm_b200.ep import local_plan
+    rng = np.random.default_rng(1)
+    for _ in range(10):
+        G = int(rng.choice([1, 2, 4]))
+        El, T = int(rng.integers(1, 4)), int(rng.integers(0, 20))
+        Etot = G * El
+        k = min(2, Etot)
+        idx = [np.stack([rng.choice(Etot, size=k, replace=False) for _ in range(T)]).astype(np.int32)
+               if T else np.zeros((0, k), np.int32) for _ in range(G)]
+        # each source's grouping order: by expert, ties by pick index (a stable sort)
+        order = []
+        for s in range(G):
+            flat = idx[s].reshape(-1)
+            srt = np.argsort(flat, kind="stable")
+            inv = np.empty_like(srt)
+            inv[srt] = np.arange(len(srt))
+            order.append(inv)
+        plans = O.ep_receive_plan(idx, order, Etot)
+        for d in range(G):
+            rows, counts = plans[d]
+            rec = np.array([[int((idx[s].reshape(-1) == d * El + j).sum()) for j in range(El)] for s in range(G)])
+            lc, lo, sorted_rows, inv = local_plan(rec)
+            assert counts.tolist() == lc.tolist()
+            # the all-to-all receive buffer: source after source, each source's rows in its grouping order
+            buf = []
+            for s in range(G):
+                flat = idx[s].reshape(-1)
+                mine = [p for p in np.argsort(order[s], kind="stable") if d * El <= flat[p] < (d + 1) * El]
+                buf.extend((s, int(p)) for p in mine)
+            assert [buf[q] for q in sorted_rows] == rows
+
+
 def test_ep_two_gloo_ranks_match_the_oracle():
     res = _run(2)
     for r in range(2):

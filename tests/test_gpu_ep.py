@@ -1,8 +1,12 @@
-"""Expert parallelism on 2 GPUs: NCCL ranks run ep.EPLayer over the
-library's kernels (each rank holding half of the experts) and every rank's
-output must match one GPU running the whole layer over all ranks' tokens
-(1e-5 of each row's max on the decode path, 2e-3 when the grouped GEMMs run).
-Skipped with fewer than 2 GPUs."""
+"""Expert parallelism: NCCL ranks (one process per GPU) run the ep layers
+over the library's kernels, each rank holding its slice of the experts, and
+every rank's output must match one GPU running the whole layer over all
+ranks' tokens (1e-5 of each row's max on the decode path, 2e-3 when the
+grouped GEMMs run).  The all-to-all and all-gather forms need 2 GPUs; the
+peer-memory form (EPPeerLayer) also runs as a single rank, and its kernels'
+multi-rank plan is checked on one GPU with emulated ranks (every rank's
+dispatch, GEMMs and combine in turn over buffers of the same device, so
+nothing waits on another launch)."""
 
 import datetime
 import os
@@ -61,9 +65,9 @@ def _worker(rank, world, port, q, E, H, I, T, mode):
             layer = EPLayer(DeviceOps(rt, local, E, 2), E, 2, H)
             out = layer(x).cpu().numpy()
             out2 = layer(x).cpu().numpy()
-        else:                          # all-gather form, eager and as a captured CUDA graph
-            from distributedmoellm_b200.ep import EPGatherLayer
-            layer = EPGatherLayer(rt, local, E, 2)
+        else:                          # all-gather / peer form, eager and as a captured CUDA graph
+            from distributedmoellm_b200.ep import EPGatherLayer, EPPeerLayer
+            layer = (EPGatherLayer if mode == "gather" else EPPeerLayer)(rt, local, E, 2)
             out = layer(x).clone().cpu().numpy()
             g = layer.capture(x)
             g.replay()
@@ -71,6 +75,8 @@ def _worker(rank, world, port, q, E, H, I, T, mode):
             out2 = layer.buffers(T).out.cpu().numpy()
             assert layer.status(T) == 0
             del g
+            if mode == "peer":
+                layer.close()
         ref = None
         if rank == 0:                  # the whole layer on one GPU over every rank's tokens
             full = LayerExperts(E, H, I, 32, L.FMT_Q4_F16, L.FMT_Q4_F16, dev)
@@ -88,23 +94,17 @@ def _worker(rank, world, port, q, E, H, I, T, mode):
         q.put((rank, "exception", repr(exc)))
 
 
-@pytest.mark.parametrize("mode,E,H,I,T,tol", [("a2a", 8, 256, 256, 12, 1e-5), ("a2a", 8, 512, 256, 512, 2e-3),
-                                                ("gather", 8, 256, 256, 12, 1e-5)],
-                         ids=["decode", "grouped_gemm", "gather_decode"])
-def test_ep_two_gpus_match_one_gpu(mode, E, H, I, T, tol):
-    import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+def _run_ranks(world, mode, E, H, I, T, tol):
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, E, H, I, T, mode)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, E, H, I, T, mode)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
     try:
-        for _ in range(2):
+        for _ in range(world):
             r, kind, val = q.get(timeout=300)
             res[r] = (kind, val)
     finally:
@@ -112,12 +112,110 @@ def test_ep_two_gpus_match_one_gpu(mode, E, H, I, T, tol):
             p.join(timeout=60)
             if p.is_alive():
                 p.kill()
-    assert all(res[r][0] == "ok" for r in range(2)), {r: res[r][1] for r in res if res[r][0] != "ok"}
+    assert all(res[r][0] == "ok" for r in range(world)), {r: res[r][1] for r in res if res[r][0] != "ok"}
     ref, gemm = res[0][1][2]
     assert gemm == (T > 100)
-    for r in range(2):
+    for r in range(world):
         out, out2 = res[r][1][0], res[r][1][1]
         want = ref[r * T:(r + 1) * T]
         err = float((np.abs(out - want).max(axis=1) / np.abs(want).max(axis=1)).max())
         assert err < tol, (r, err)
-        assert np.array_equal(out, out2)      # repeat (a2a) / graph replay (gather) is bit-identical
+        assert np.array_equal(out, out2)      # repeat (a2a) / graph replay (gather, peer) is bit-identical
+
+
+@pytest.mark.parametrize("mode,E,H,I,T,tol", [("a2a", 8, 256, 256, 12, 1e-5), ("a2a", 8, 512, 256, 512, 2e-3),
+                                                ("gather", 8, 256, 256, 12, 1e-5)],
+                         ids=["decode", "grouped_gemm", "gather_decode"])
+def test_ep_two_gpus_match_one_gpu(mode, E, H, I, T, tol):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    _run_ranks(2, mode, E, H, I, T, tol)
+
+
+@pytest.mark.parametrize("world", [1, 2])
+def test_ep_peer_layer_matches_one_gpu(world):
+    import torch
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    _run_ranks(world, "peer", 8, 512, 256, 512, 2e-3)
+
+
+@pytest.mark.parametrize("G,T", [(2, 300), (4, 160)])
+def test_peer_dispatch_with_emulated_ranks_on_one_gpu(G, T):
+    """G ranks on one GPU: each rank's routing, mb_ep_dispatch into the G
+    receive buffers, each rank's grouped GEMMs storing results through the
+    return addresses, each rank's combine.  The received rows must follow the
+    oracle's receive plan, and the outputs match one GPU running the layer
+    over all tokens (2e-3 of each row's max: both are the grouped GEMMs)."""
+    import torch
+    sys.path.insert(0, str(ROOT))
+    import oracle as O
+    from distributedmoellm_b200 import _build
+    from distributedmoellm_b200 import device as D
+    from distributedmoellm_b200 import layout as L
+    from distributedmoellm_b200.layer import MoELayer
+    from distributedmoellm_b200.store import LayerExperts
+    _build.build()
+    D.require_device()
+    E, H, I, k = 8, 512, 256, 2
+    dev = torch.device("cuda", 0)
+    parts, router = _setup(E, H, I)
+    rt = torch.from_numpy(router).to(dev)
+    El, P = E // G, T * k
+    cap = G * P
+    i32 = dict(dtype=torch.int32, device=dev)
+    rows = [torch.zeros((cap, H), dtype=torch.float16, device=dev) for _ in range(G)]
+    rexp = [torch.zeros(cap, **i32) for _ in range(G)]
+    ret = [torch.full((cap,), -1, **i32) for _ in range(G)]
+    yh = [torch.zeros((P, H), dtype=torch.float32, device=dev) for _ in range(G)]
+
+    def table(ts):
+        return torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device=dev)
+    status = torch.zeros(1, **i32)
+    xs, idx, w, rexp_own, rts = [], [], [], [], []
+    for s in range(G):
+        x = torch.from_numpy(_tokens(s, T, H)).to(dev)
+        i, ww = torch.empty((T, k), **i32), torch.empty((T, k), dtype=torch.float32, device=dev)
+        re = torch.empty(T, **i32)
+        D.router_route(x, rt, k, True, i, ww, row_exp=re)
+        xs.append(x), idx.append(i), w.append(ww), rexp_own.append(re), rts.append(D.permute(i, ww, E))
+    counts_all = torch.stack([r.counts for r in rts]).contiguous()
+    lc = [torch.zeros(El, **i32) for _ in range(G)]
+    lo = [torch.zeros(El + 1, **i32) for _ in range(G)]
+    for s in range(G):
+        D.ep_dispatch(xs[s], rexp_own[s], idx[s], rts[s], counts_all, s, table(rows), table(rexp), table(ret), cap,
+                      lc[s], lo[s], status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    plans = O.ep_receive_plan([i.cpu().numpy() for i in idx], [r.inv[:P].cpu().numpy() for r in rts], E)
+    for d in range(G):
+        want_rows, want_counts = plans[d]
+        n = len(want_rows)
+        assert lc[d].cpu().numpy().tolist() == want_counts.tolist()
+        assert lo[d].cpu().numpy().tolist() == [0] + np.cumsum(want_counts).tolist()
+        got = ret[d][:n].cpu().numpy().astype(np.int64)
+        assert [(int(v) >> 24, int(v) & 0xFFFFFF) for v in got] == want_rows
+        assert (ret[d][n:].cpu().numpy() == -1).all()          # nothing past the received rows
+        re_want = np.array([rexp_own[s][p // k].item() for s, p in want_rows[:64]], np.int32)
+        assert (rexp[d][:min(n, 64)].cpu().numpy() == re_want).all()
+    for d in range(G):
+        local = LayerExperts(El, H, I, 32, L.FMT_Q4_F16, L.FMT_Q4_F16, dev)
+        for j in range(El):
+            local.put_int4(j, *parts[d * El + j])
+        local.publish()
+        ws = torch.empty(D.prefill_rows_workspace_bytes(cap, I), dtype=torch.uint8, device=dev)
+        D.moe_prefill_rows(local, rows[d].data_ptr(), rexp[d].data_ptr(), lc[d], lo[d], cap, ws,
+                           y_ret=ret[d].data_ptr(), y_peers=table(yh), peer_rows=P, status=status)
+    ident = torch.arange(P, **i32)
+    outs = [D.combine(yh[s], ident, w[s].view(-1), T, k).cpu().numpy() for s in range(G)]
+    assert int(status.item()) == 0
+    full = LayerExperts(E, H, I, 32, L.FMT_Q4_F16, L.FMT_Q4_F16, dev)
+    for e in range(E):
+        full.put_int4(e, *parts[e])
+    full.publish()
+    ml = MoELayer(rt, full, k, True, gemm_min_rows=1)
+    ref = ml(torch.cat(xs)).cpu().numpy()
+    got = np.concatenate(outs)
+    err = float((np.abs(got - ref).max(axis=1) / np.abs(ref).max(axis=1)).max())
+    assert err < 2e-3, err
