@@ -604,6 +604,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint32_t r[32];
                     tmem_ld32(acol + cb, r);
                     if (!ok) continue;
+                    // the block's 32 tokens' scales (and output rows): lane i holds token cb + i's, passed to
+                    // the other lanes by shuffles -- reading them from shared memory between the global stores
+                    // would serialise each read behind the previous store (the compiler cannot rule out that
+                    // a store changes them)
+                    const float tsv = ts[cb + lane] * wunscale;
                     if (a.phase == 1 && a.pre) {
                         // precise gate|up: lanes s < 16 hold gate row j, lanes 16 + s the up row j; their true
                         // values go to pre[pick][j] and pre[pick][I + j], written or added
@@ -613,9 +618,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int i = 0; i < 32; ++i) {
                             const int n = cb + i;
+                            const float v = __uint_as_float(r[i]) * __shfl_sync(0xffffffffu, tsv, i);
                             if (n < nrows && j < a.O_real) {
                                 float* dst = a.pre + (int64_t)(w.off_e + n0 + n) * (2 * a.O_real) + col;
-                                const float v = __uint_as_float(r[i]) * ts[n] * wunscale;
                                 *dst = a.accumulate ? *dst + v : v;
                             }
                         }
@@ -627,15 +632,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const bool hi = lane >= 16;
                         const int j = w.mb * 64 + 16 * q + s;
                         const int jpos = (j & ~7) + 2 * (s & 3);
+                        const float tav = ta[cb + lane];
 #pragma unroll
                         for (int i = 0; i < 32; i += 2) {
                             const float other =
                                 __uint_as_float(__shfl_xor_sync(0xffffffffu, hi ? r[i] : r[i + 1], 16));
-                            const int n = cb + i + (hi ? 1 : 0);
-                            const float f = ts[n] * wunscale;
+                            const int ni = i + (hi ? 1 : 0);
+                            const int n = cb + ni;
+                            const float f = __shfl_sync(0xffffffffu, tsv, ni);
                             const float gv = (hi ? other : __uint_as_float(r[i])) * f;
                             const float uv = (hi ? __uint_as_float(r[i + 1]) : other) * f;
-                            const float act = __fdividef(gv, 1.0f + __expf(-gv)) * uv * ta[n];
+                            const float act =
+                                __fdividef(gv, 1.0f + __expf(-gv)) * uv * __shfl_sync(0xffffffffu, tav, ni);
                             const float act4 = __shfl_xor_sync(0xffffffffu, act, 4);
                             if ((s & 4) == 0 && n < nrows && j < a.O_real)
                                 *reinterpret_cast<uint32_t*>(a.act + (int64_t)(w.off_e + n0 + n) * a.O_real + jpos) =
@@ -643,11 +651,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     } else {
                         const int o = w.mb * kBM + L;
-                        float* const* ty = tok_y + slot * kMaxN;
+                        const unsigned long long rowp =
+                            reinterpret_cast<unsigned long long>(tok_y[slot * kMaxN + cb + lane]);
 #pragma unroll
                         for (int i = 0; i < 32; ++i) {
                             const int n = cb + i;
-                            if (n < nrows && o < a.O_real && ty[n]) ty[n][o] = __uint_as_float(r[i]) * ts[n] * wunscale;
+                            float* dst = reinterpret_cast<float*>(__shfl_sync(0xffffffffu, rowp, i));
+                            const float v = __uint_as_float(r[i]) * __shfl_sync(0xffffffffu, tsv, i);
+                            if (n < nrows && o < a.O_real && dst) dst[o] = v;
                         }
                     }
                 }
