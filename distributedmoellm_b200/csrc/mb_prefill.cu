@@ -633,32 +633,55 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int j = w.mb * 64 + 16 * q + s;
                         const int jpos = (j & ~7) + 2 * (s & 3);
                         const float tav = ta[cb + lane];
+                        // batches of 8 token pairs: all shuffles, then the math, then the stores, so that the
+                        // eight independent chains overlap (one epilogue warp per scheduler has nothing else
+                        // to hide their latency with)
 #pragma unroll
-                        for (int i = 0; i < 32; i += 2) {
-                            const float other =
-                                __uint_as_float(__shfl_xor_sync(0xffffffffu, hi ? r[i] : r[i + 1], 16));
-                            const int ni = i + (hi ? 1 : 0);
-                            const int n = cb + ni;
-                            const float f = __shfl_sync(0xffffffffu, tsv, ni);
-                            const float gv = (hi ? other : __uint_as_float(r[i])) * f;
-                            const float uv = (hi ? __uint_as_float(r[i + 1]) : other) * f;
-                            const float act =
-                                __fdividef(gv, 1.0f + __expf(-gv)) * uv * __shfl_sync(0xffffffffu, tav, ni);
-                            const float act4 = __shfl_xor_sync(0xffffffffu, act, 4);
-                            if ((s & 4) == 0 && n < nrows && j < a.O_real)
-                                *reinterpret_cast<uint32_t*>(a.act + (int64_t)(w.off_e + n0 + n) * a.O_real + jpos) =
-                                    pack_f16(act, act4);
+                        for (int i0 = 0; i0 < 32; i0 += 16) {
+                            float gv[8], uv[8], tk[8];
+#pragma unroll
+                            for (int k = 0; k < 8; ++k) {
+                                const int i = i0 + 2 * k, ni = i + (hi ? 1 : 0);
+                                const float other =
+                                    __uint_as_float(__shfl_xor_sync(0xffffffffu, hi ? r[i] : r[i + 1], 16));
+                                const float f = __shfl_sync(0xffffffffu, tsv, ni);
+                                tk[k] = __shfl_sync(0xffffffffu, tav, ni);
+                                gv[k] = (hi ? other : __uint_as_float(r[i])) * f;
+                                uv[k] = (hi ? __uint_as_float(r[i + 1]) : other) * f;
+                            }
+                            float act[8];
+#pragma unroll
+                            for (int k = 0; k < 8; ++k)
+                                act[k] = __fdividef(gv[k], 1.0f + __expf(-gv[k])) * uv[k] * tk[k];
+                            uint32_t pk[8];
+#pragma unroll
+                            for (int k = 0; k < 8; ++k) pk[k] = pack_f16(act[k], __shfl_xor_sync(0xffffffffu, act[k], 4));
+#pragma unroll
+                            for (int k = 0; k < 8; ++k) {
+                                const int n = cb + i0 + 2 * k + (hi ? 1 : 0);
+                                if ((s & 4) == 0 && n < nrows && j < a.O_real)
+                                    *reinterpret_cast<uint32_t*>(a.act + (int64_t)(w.off_e + n0 + n) * a.O_real +
+                                                                 jpos) = pk[k];
+                            }
                         }
                     } else {
                         const int o = w.mb * kBM + L;
                         const unsigned long long rowp =
                             reinterpret_cast<unsigned long long>(tok_y[slot * kMaxN + cb + lane]);
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            const int n = cb + i;
-                            float* dst = reinterpret_cast<float*>(__shfl_sync(0xffffffffu, rowp, i));
-                            const float v = __uint_as_float(r[i]) * __shfl_sync(0xffffffffu, tsv, i);
-                            if (n < nrows && o < a.O_real && dst) dst[o] = v;
+                        for (int i0 = 0; i0 < 32; i0 += 8) {   // batches of 8 tokens: shuffles, then stores
+                            float* dst[8];
+                            float v[8];
+#pragma unroll
+                            for (int k = 0; k < 8; ++k) {
+                                dst[k] = reinterpret_cast<float*>(__shfl_sync(0xffffffffu, rowp, i0 + k));
+                                v[k] = __uint_as_float(r[i0 + k]) * __shfl_sync(0xffffffffu, tsv, i0 + k);
+                            }
+#pragma unroll
+                            for (int k = 0; k < 8; ++k) {
+                                const int n = cb + i0 + k;
+                                if (n < nrows && o < a.O_real && dst[k]) dst[k][o] = v[k];
+                            }
                         }
                     }
                 }
