@@ -258,6 +258,17 @@ __device__ __forceinline__ void rotate_back(uint4 (&v)[4], int rot)
     for (int t = 0; t < 4; ++t) v[t] = r2 ? u[(t + 2) & 3] : u[t];
 }
 
+// v[k] = p[2k + odd], k < 8, from 16 floats of shared memory (16-byte aligned) in four vector reads.
+__device__ __forceinline__ void load_alt8(const float* p, bool odd, float (&v)[8])
+{
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const float4 t = *reinterpret_cast<const float4*>(p + 4 * c);
+        v[2 * c] = odd ? t.y : t.x;
+        v[2 * c + 1] = odd ? t.w : t.z;
+    }
+}
+
 // ---- the GEMM kernel ----------------------------------------------------------------
 
 template <int FMT>
@@ -604,17 +615,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint32_t r[32];
                     tmem_ld32(acol + cb, r);
                     if (!ok) continue;
-                    // the block's 32 tokens' scales (and output rows): lane i holds token cb + i's, passed to
-                    // the other lanes by shuffles -- reading them from shared memory between the global stores
-                    // would serialise each read behind the previous store (the compiler cannot rule out that
-                    // a store changes them)
-                    const float tsv = ts[cb + lane] * wunscale;
+                    // Batches of 8 tokens (8 token pairs in phase 1): first the batch's scales (and output
+                    // rows) as broadcast reads of shared memory, then the values, then the stores, so the eight
+                    // independent chains overlap (one epilogue warp per scheduler has nothing else to hide
+                    // their latency with).  Reads placed between the global stores would each wait behind the
+                    // previous store (the compiler cannot rule out that a store changes them).
                     if (a.phase == 1 && a.pre) {
                         // precise gate|up: lanes s < 16 hold gate row j, lanes 16 + s the up row j; their true
                         // values go to pre[pick][j] and pre[pick][I + j], written or added
                         const int s = lane & 15;
                         const int j = w.mb * 64 + 16 * q + s;
                         const int col = (lane >= 16 ? a.O_real : 0) + j;
+                        const float tsv = ts[cb + lane] * wunscale;
 #pragma unroll
                         for (int i = 0; i < 32; ++i) {
                             const int n = cb + i;
@@ -632,27 +644,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const bool hi = lane >= 16;
                         const int j = w.mb * 64 + 16 * q + s;
                         const int jpos = (j & ~7) + 2 * (s & 3);
-                        const float tav = ta[cb + lane];
-                        // batches of 8 token pairs: all shuffles, then the math, then the stores, so that the
-                        // eight independent chains overlap (one epilogue warp per scheduler has nothing else
-                        // to hide their latency with)
 #pragma unroll
                         for (int i0 = 0; i0 < 32; i0 += 16) {
-                            float gv[8], uv[8], tk[8];
+                            float tsk[8], tak[8];
+                            load_alt8(ts + cb + i0, hi, tsk);
+                            load_alt8(ta + cb + i0, hi, tak);
+                            float gv[8], uv[8];
 #pragma unroll
                             for (int k = 0; k < 8; ++k) {
-                                const int i = i0 + 2 * k, ni = i + (hi ? 1 : 0);
+                                const int i = i0 + 2 * k;
                                 const float other =
                                     __uint_as_float(__shfl_xor_sync(0xffffffffu, hi ? r[i] : r[i + 1], 16));
-                                const float f = __shfl_sync(0xffffffffu, tsv, ni);
-                                tk[k] = __shfl_sync(0xffffffffu, tav, ni);
+                                const float f = tsk[k] * wunscale;
                                 gv[k] = (hi ? other : __uint_as_float(r[i])) * f;
                                 uv[k] = (hi ? __uint_as_float(r[i + 1]) : other) * f;
                             }
                             float act[8];
 #pragma unroll
                             for (int k = 0; k < 8; ++k)
-                                act[k] = __fdividef(gv[k], 1.0f + __expf(-gv[k])) * uv[k] * tk[k];
+                                act[k] = __fdividef(gv[k], 1.0f + __expf(-gv[k])) * uv[k] * tak[k];
                             uint32_t pk[8];
 #pragma unroll
                             for (int k = 0; k < 8; ++k) pk[k] = pack_f16(act[k], __shfl_xor_sync(0xffffffffu, act[k], 4));
@@ -666,21 +676,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     } else {
                         const int o = w.mb * kBM + L;
-                        const unsigned long long rowp =
-                            reinterpret_cast<unsigned long long>(tok_y[slot * kMaxN + cb + lane]);
+                        float* const* ty = tok_y + slot * kMaxN + cb;
 #pragma unroll
-                        for (int i0 = 0; i0 < 32; i0 += 8) {   // batches of 8 tokens: shuffles, then stores
+                        for (int i0 = 0; i0 < 32; i0 += 8) {
+                            const float4 s0 = *reinterpret_cast<const float4*>(ts + cb + i0);
+                            const float4 s1 = *reinterpret_cast<const float4*>(ts + cb + i0 + 4);
+                            const float sc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
                             float* dst[8];
-                            float v[8];
 #pragma unroll
-                            for (int k = 0; k < 8; ++k) {
-                                dst[k] = reinterpret_cast<float*>(__shfl_sync(0xffffffffu, rowp, i0 + k));
-                                v[k] = __uint_as_float(r[i0 + k]) * __shfl_sync(0xffffffffu, tsv, i0 + k);
+                            for (int c = 0; c < 4; ++c) {
+                                const ulonglong2 pp = *reinterpret_cast<const ulonglong2*>(ty + i0 + 2 * c);
+                                dst[2 * c] = reinterpret_cast<float*>(pp.x);
+                                dst[2 * c + 1] = reinterpret_cast<float*>(pp.y);
                             }
 #pragma unroll
                             for (int k = 0; k < 8; ++k) {
                                 const int n = cb + i0 + k;
-                                if (n < nrows && o < a.O_real && dst[k]) dst[k][o] = v[k];
+                                const float v = __uint_as_float(r[i0 + k]) * sc[k] * wunscale;
+                                if (n < nrows && o < a.O_real && dst[k]) dst[k][o] = v;
                             }
                         }
                     }
