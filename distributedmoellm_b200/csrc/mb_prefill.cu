@@ -63,6 +63,7 @@ static_assert(kAccCol + 2 * kMaxN <= kTmemCols, "TMEM columns");
 constexpr int kDqWarps = 8;    // warps 4..11: two sets of four (one per TMEM lane quarter), alternate quads
 constexpr int kEpiWarps = 4;   // warps 12..15
 constexpr int kThreads = 512;
+static_assert(kMaxMetaE <= kThreads && kThreads <= 32 * 32, "one expert per thread in the item scan");
 constexpr int kBHalf = kMaxN * 128;   // bytes of one half (64 columns) of a token stage
 // Token tiles: one TMA box per 64-column half, from the tensor map whose box is the pass's token count
 // rounded up to kBoxStep rows (one instruction per half instead of one per 32 rows; a box never
@@ -85,6 +86,7 @@ struct PrefillArgs {
     int RT;                    // row tiles of the matrix
     int MB;                    // M blocks (8 row tiles) per expert
     int block_bytes;
+    int max_items;             // an upper bound of the launch's items (sizes the grid)
     const int32_t* counts;
     const int32_t* offsets;
     const int32_t* sorted_rows;   // the token row of each pick, or null: pick p is row p
@@ -198,33 +200,35 @@ __device__ __forceinline__ uint32_t idesc_f16(int n)
 }
 
 // The static sequence of work items every role of a CTA walks: items
-// blockIdx.x, blockIdx.x + gridDim.x, ... of E * MB, skipping experts
-// outside this launch.
-// meta[e] = (picks, first pick, this launch's weight exponent, activation exponent base), staged in
-// shared memory once per CTA.
+// blockIdx.x, blockIdx.x + gridDim.x, ... of all (expert, pass of at most kMaxN
+// picks, M block) of the experts in this launch, expert-major, then pass, then
+// M block (so items that run at the same time share their token rows).  One
+// item is one pass; an expert with many picks spreads its passes over many CTAs.
+// meta[e] = (picks, first pick, this launch's weight exponent, activation exponent base) and
+// pstart[e] = the first item of expert e (pstart[E] = all items), in shared memory once per CTA.
 struct Items {
     const PrefillArgs& a;
     const int4* meta;
+    const int* pstart;
     int it;
-    int e, mb, n_e, off_e, passes, wexp, aexp;
-    __device__ Items(const PrefillArgs& args, const int4* m) : a(args), meta(m), it((int)blockIdx.x - (int)gridDim.x) {}
+    int e, mb, n_e, off_e, passes, pass0, wexp, aexp;
+    __device__ Items(const PrefillArgs& args, const int4* m, const int* ps)
+        : a(args), meta(m), pstart(ps), it((int)blockIdx.x - (int)gridDim.x), e(0) {}
     __device__ bool next()
     {
-        for (;;) {
-            it += gridDim.x;
-            if (it >= a.E * a.MB) return false;
-            e = it / a.MB;
-            mb = it - e * a.MB;
-            const int4 m = meta[e];
-            n_e = m.x;
-            if (n_e >= a.min_rows && n_e > 0) {
-                off_e = m.y;
-                wexp = m.z;
-                aexp = m.w;
-                passes = (n_e + kMaxN - 1) / kMaxN;
-                return true;
-            }
-        }
+        it += gridDim.x;
+        if (it >= pstart[a.E]) return false;
+        while (pstart[e + 1] <= it) ++e;   // items only move forward: the expert whose items hold it
+        const int local = it - pstart[e];
+        pass0 = local / a.MB;
+        mb = local - pass0 * a.MB;
+        const int4 m = meta[e];
+        n_e = m.x;
+        off_e = m.y;
+        wexp = m.z;
+        aexp = m.w;
+        passes = 1;
+        return true;
     }
 };
 
@@ -300,6 +304,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     int4* meta = reinterpret_cast<int4*>(tmem_slot + 4);       // [E]
+    int* pstart = reinterpret_cast<int*>(meta + a.E);          // [E + 1]
+    int* wsum = pstart + a.E + 1;                              // [16] scan of the warps' item counts
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int e = threadIdx.x; e < a.E; e += kThreads) {
@@ -330,6 +336,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    {
+        // pstart: exclusive scan of the experts' item counts (MB items per pass of at most kMaxN picks) over
+        // the block, one expert per thread (E <= kMaxMetaE == kThreads)
+        int v = 0;
+        if ((int)threadIdx.x < a.E) {
+            const int n = meta[threadIdx.x].x;
+            v = (n >= a.min_rows && n > 0) ? a.MB * ((n + kMaxN - 1) / kMaxN) : 0;
+        }
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, v, o);
+            if (lane >= o) v += t;
+        }
+        if (lane == 31) wsum[warp] = v;
+        __syncthreads();
+        if (warp == 0) {
+            int s = lane < kThreads / 32 ? wsum[lane] : 0;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, s, o);
+                if (lane >= o) s += t;
+            }
+            if (lane < kThreads / 32) wsum[lane] = s;
+        }
+        __syncthreads();
+        if ((int)threadIdx.x < a.E) pstart[threadIdx.x + 1] = v + (warp > 0 ? wsum[warp - 1] : 0);
+        if (threadIdx.x == 0) pstart[0] = 0;
+        __syncthreads();
+    }
     const uint32_t tmem = *tmem_slot;
     const int KH = a.KH;
     const int quads = (KH + 1) >> 1;   // quads per pass; the last one has one half when KH is odd
@@ -339,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ------------------------------------------------------------ weight producer
         {
-            Items w(a, meta);
+            Items w(a, meta, pstart);
             int gq = 0;
             bool ok = true;
             while (ok && w.next() && !*abort_flag) {
@@ -366,12 +401,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------ token producer
         {
-            Items w(a, meta);
+            Items w(a, meta, pstart);
             int gq = 0;
             bool ok = true;
             while (ok && w.next() && !*abort_flag) {
                 for (int pass = 0; ok && pass < w.passes; ++pass) {
-                    const int n0 = pass * kMaxN;
+                    const int n0 = (w.pass0 + pass) * kMaxN;
                     const int nrows = min(kMaxN, w.n_e - n0);
                     const int nbox = (((nrows + 15) & ~15) + kBoxStep - 1) / kBoxStep;   // box height / kBoxStep
                     const CUtensorMap* bmap = &bmaps.m[nbox - 1];
@@ -393,13 +428,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 2) {
         // ------------------------------------------------------------ MMA issuer (whole warp, one lane issues)
-        Items w(a, meta);
+        Items w(a, meta, pstart);
         int gq = 0;
         int64_t np = 0;   // passes issued (accumulator buffer np & 1)
         bool ok = true;
         while (ok && w.next()) {
             for (int pass = 0; ok && pass < w.passes; ++pass, ++np) {
-                const int nrows = min(kMaxN, w.n_e - pass * kMaxN);
+                const int nrows = min(kMaxN, w.n_e - (w.pass0 + pass) * kMaxN);
                 const uint32_t idesc = idesc_f16((nrows + 15) & ~15);
                 const int slot = (int)(np & 1);
                 if (np >= 2)
@@ -444,7 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             trow = L & 15;
         }
         const uint32_t taddr0 = tmem + ((uint32_t)(32 * q) << 16);
-        Items w(a, meta);
+        Items w(a, meta, pstart);
         int gq = 0;
         while (w.next()) {
             const int tiles = min(8, a.RT - w.mb * 8);
@@ -568,13 +603,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int L = 32 * q + lane;
         const int et = threadIdx.x - 32 * (4 + kDqWarps);   // 0..127
         const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
-        Items w(a, meta);
+        Items w(a, meta, pstart);
         int64_t np = 0;
         while (w.next()) {
             const float wunscale = pow2i(-clamp120(w.wexp));
             for (int pass = 0; pass < w.passes; ++pass, ++np) {
                 const int slot = (int)(np & 1);
-                const int n0 = pass * kMaxN;
+                const int n0 = (w.pass0 + pass) * kMaxN;
                 const int nrows = min(kMaxN, w.n_e - n0);
                 const int npad = (nrows + 15) & ~15;
                 float* ts = tok_s + slot * kMaxN;
@@ -824,7 +859,7 @@ size_t smem_bytes(int fmt, int block_bytes, int E)
 {
     const int ps = pstages(fmt == MB_FMT_Q8_F16 || fmt == MB_FMT_Q8_F32);
     return 1024 + (size_t)kBStages * 2 * kBHalf + (size_t)ps * 8 * block_bytes + 4 * kMaxN * 4 + 2 * kMaxN * 8 +
-           (2 * kBStages + 2 * ps + 2 * kASlots + 4) * 8 + 16 + (size_t)E * 16;
+           (2 * kBStages + 2 * ps + 2 * kASlots + 4) * 8 + 16 + (size_t)E * 16 + (size_t)(E + 1) * 4 + 16 * 4;
 }
 
 template <int FMT>
@@ -843,8 +878,7 @@ int launch(const PrefillArgs& a, const TokenMaps& maps, cudaStream_t st)
         }
         set[dev & 63] = smem;
     }
-    const int items = a.E * a.MB;
-    const int grid = items < mb_num_sms() ? items : mb_num_sms();
+    const int grid = std::max(1, std::min(a.max_items, mb_num_sms()));
     kern<<<grid, kThreads, smem, st>>>(a, maps);
     return mb_check_launch("mb_moe_prefill");
 }
@@ -863,6 +897,12 @@ int dispatch(int fmt, const PrefillArgs& a, const TokenMaps& map, cudaStream_t s
 
 int64_t r1k(int64_t n) { return (n + 1023) / 1024 * 1024; }
 
+// At most MB * (E + P / kMaxN) items: every expert's passes over P picks in all.
+int items_bound(int MB, int E, int64_t P)
+{
+    return (int)std::min<int64_t>((int64_t)MB * (E + (P + kMaxN - 1) / kMaxN), 1 << 30);
+}
+
 // The GEMM launches of one layer over tokens already in f16 rows xp (P x H, pick order, K-permuted, each
 // scaled by 2^row_exp): gate|up into a.act (with the precise three-product form when fmt_gu is
 // MB_FMT_Q4K_F32: xp_lo the residual rows, pre the f32 pre-activations), then down into the output rows.
@@ -878,6 +918,7 @@ int run_gemms(PrefillArgs a, int H, int I, int fmt_gu, int fmt_down, const __hal
     a.KH = H / 64;
     a.RT = I / 8;
     a.MB = (a.RT + 7) / 8;
+    a.max_items = items_bound(a.MB, a.E, P);
     a.block_bytes = block_bytes_of(fmt_gu);
     a.O_real = I;
     if (fmt_gu != MB_FMT_Q4K_F32) {
@@ -913,6 +954,7 @@ int run_gemms(PrefillArgs a, int H, int I, int fmt_gu, int fmt_down, const __hal
     a.KH = I / 64;
     a.RT = H / 16;
     a.MB = (a.RT + 7) / 8;
+    a.max_items = items_bound(a.MB, a.E, P);
     a.block_bytes = block_bytes_of(fmt_down);
     a.O_real = H;
     return dispatch(fmt_down, a, map, st);
