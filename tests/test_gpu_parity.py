@@ -101,7 +101,7 @@ def test_router_topk_matches_reference(D, golden, case):
 
 
 @pytest.mark.parametrize("T,H,E,k", [(1, 2048, 128, 8), (37, 2048, 128, 8), (64, 256, 16, 2), (300, 4096, 8, 2),
-                                     (5, 200, 60, 6)])
+                                     (5, 200, 60, 6), (600, 2048, 128, 8), (777, 1000, 60, 6), (2048, 2048, 128, 8)])
 def test_router_logits_and_route(D, T, H, E, k):
     rng = np.random.default_rng(T + H)
     x = rng.standard_normal((T, H)).astype(np.float32)
