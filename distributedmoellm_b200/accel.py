@@ -23,7 +23,7 @@ import torch
 
 from . import device as D
 from .layer import GEMM_MIN_ROWS, run_experts
-from .packing import pack_expert
+from .packing import pack_expert, pack_expert_on
 
 
 _TORCH_DTYPE = {"<i4": torch.int32, "<i8": torch.int64, "<f4": torch.float32}
@@ -42,15 +42,25 @@ class DevicePool:
     """Packed experts, each in its own device buffer (gate|up tiles, down tiles)."""
 
     def __init__(self, device):
-        self.device = torch.device(device)
+        d = torch.device(device)
+        if d.type == "cuda" and d.index is None:      # "cuda": the current device, by its index
+            d = torch.device("cuda", torch.cuda.current_device())
+        self.device = d
         self.entries: dict = {}          # key -> (Packed, buffer, gu address, down address)
         self._ws: dict = {}
         self._ws_lock = threading.Lock()
         self._pin = None            # pinned staging buffer of compute()'s routing arrays, and its device twin
         self._dev_stage = None
         self._stage_done = None     # recorded after the last copy out of the pinned buffer
+        self._result = None         # pinned buffer a caller reads results back through (result_buffer)
 
     def put(self, key, packed) -> int:
+        buf = getattr(packed, "buf", None)
+        if buf is not None:      # laid out on this device already (packing.pack_expert_on)
+            if buf.device != self.device:
+                raise ValueError(f"expert {key} was packed on {buf.device}, this pool is on {self.device}")
+            self.entries[key] = (packed, buf, buf.data_ptr(), buf.data_ptr() + packed.dn_offset)
+            return buf.numel()
         g = torch.from_numpy(np.ascontiguousarray(packed.gu_tiles))
         d = torch.from_numpy(np.ascontiguousarray(packed.dn_tiles))
         off = (g.numel() + 255) // 256 * 256
@@ -73,6 +83,20 @@ class DevicePool:
             if b is None or b.numel() < nbytes:
                 b = self._ws[name] = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=self.device)
             return b
+
+    def read_back(self, part: torch.Tensor, status: torch.Tensor):
+        """(part as a host array, the status word): both come back through one
+        pinned buffer with one wait on the current stream.  The array is a view
+        of that buffer, valid until the next read_back (the caller serialises
+        its calls on this pool)."""
+        n = part.numel()
+        if self._result is None or self._result.numel() < n + 1:
+            self._result = torch.empty(max(n + 1, 1 << 14), dtype=torch.float32).pin_memory()
+        hp, hs = self._result[:n].view(part.shape), self._result[n:n + 1].view(torch.int32)
+        hp.copy_(part, non_blocking=True)
+        hs.copy_(status.view(torch.int32).reshape(1), non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return hp.numpy(), int(hs.item())
 
     def _stage(self, arrays):
         """Copy the given small host arrays to the device in one transfer through
@@ -129,25 +153,30 @@ class DevicePool:
         host = [order, all_w[order], row_ptr]
         plan = []
         for sig, idx in sigs.items():
-            table = np.array([[self.entries[keys[i]][2], self.entries[keys[i]][3]] for i in idx], np.int64)
+            ents = [self.entries[keys[i]] for i in idx]
+            table = np.array([(en[2], en[3]) for en in ents], np.int64)
             eexp = np.zeros((len(idx), 4), np.int32)
-            eexp[:, :3] = [self.entries[keys[i]][0].eexp for i in idx]
-            c = counts[idx].astype(np.int32)
-            sel = np.concatenate([np.arange(base[i], base[i + 1]) for i in idx])
-            plan.append((sig, len(host), sel))
-            host += [table, eexp, c, np.concatenate([[0], np.cumsum(c)]).astype(np.int32),
-                     all_rows[sel].astype(np.int32), sel.astype(np.int64)]
+            eexp[:, :3] = [en[0].eexp for en in ents]
+            if len(sigs) == 1:       # one signature (the usual case): its picks are all picks, in order
+                c, sel = counts.astype(np.int32), None
+                host += [table, eexp, c, base.astype(np.int32), all_rows.astype(np.int32)]
+            else:
+                c = counts[idx].astype(np.int32)
+                sel = np.concatenate([np.arange(base[i], base[i + 1]) for i in idx])
+                host += [table, eexp, c, np.concatenate([[0], np.cumsum(c)]).astype(np.int32),
+                         all_rows[sel].astype(np.int32), sel.astype(np.int64)]
+            plan.append((sig, len(host) - (5 if sel is None else 6), sel))
         d = self._stage(host)
         for sig, j, sel in plan:
-            table, eexp, c, offs, srows, sel_d = d[j:j + 6]
+            table, eexp, c, offs, srows = d[j:j + 5]
             r = D.Routing.from_plan(c, offs, srows)
             s = _Set(*sig, table, eexp)
-            if len(plan) == 1:       # one signature (the usual case): its picks are all picks, in order
+            if sel is None:
                 run_experts(s, x, row_exp, r, y, self.workspace, status, gemm_min_rows)
             else:
                 ys = torch.empty((max(len(sel), 1), H), dtype=torch.float32, device=dev)
                 run_experts(s, x, row_exp, r, ys, self.workspace, status, gemm_min_rows)
-                y[sel_d] = ys[:len(sel)]
+                y[d[j + 5]] = ys[:len(sel)]
         part = D.combine(y, d[0], d[1], len(uniq), 1, row_ptr=d[2])
         return uniq, part, status
 
@@ -194,12 +223,14 @@ class GpuTier:
         return key in self.experts
 
     def add(self, key, expert) -> bool:
-        """Upload one moelan Expert in its packed form.  False if the tier is
-        full or the expert has no packed form (it then stays on the CPU)."""
-        packed = pack_expert(expert)
-        if packed is None or self.used + packed.nbytes > self.budget:
-            return False
-        with self.lock, torch.cuda.device(self.device):
+        """Upload one moelan Expert in its packed form: its bytes as moelan
+        holds them go to the device and the library's packers lay them out
+        there.  False if the tier is full or the expert has no packed form (it
+        then stays on the CPU)."""
+        with self.lock:
+            packed = pack_expert_on(expert, self.pool.device, max_bytes=self.budget - self.used)
+            if packed is None:
+                return False
             self.used += self.pool.put(key, packed)
             self.experts[key] = packed
         return True

@@ -23,6 +23,7 @@ from __future__ import annotations
 import ctypes
 import threading
 from collections import OrderedDict
+from types import SimpleNamespace
 
 import numpy as np
 import torch
@@ -30,7 +31,7 @@ import torch
 from . import device as D
 from . import layout
 from .accel import DevicePool
-from .packing import Packed
+from .packing import pack_expert_on
 
 _CACHE_MAX = 512
 _lock = threading.RLock()                 # guards the caches below and each call's use of them
@@ -172,18 +173,22 @@ def _moe_q4(x, items, H, I, gs, out):
     pool, order = _pool[dev.index]
     keys = []
     for ptrs, _, _ in items:
-        key = (tuple(int(p) for p in ptrs), H, I, gs)
+        key = (ptrs if type(ptrs) is tuple else tuple(int(p) for p in ptrs), H, I, gs)
         if key not in pool.entries:
             g_raw = _from_address(ptrs[0], 2 * I * H // 2, np.uint8).reshape(2 * I, H // 2)
             g_s = _from_address(ptrs[1], 2 * I * (H // gs), np.float32).reshape(2 * I, H // gs)
             d_raw = _from_address(ptrs[2], H * I // 2, np.uint8).reshape(H, I // 2)
             d_s = _from_address(ptrs[3], H * (I // gs), np.float32).reshape(H, I // gs)
             off = int(ptrs[4]) == 0
-            eexp = (layout.weight_exponent(g_s, 8), layout.weight_exponent(d_s, 8),
-                    layout.act_exponent(layout.row_l1_q4(g_raw, g_s, gs, off), I))
-            pool.put(key, Packed(layout.FMT_Q4_F32, layout.FMT_Q4_F32, gs, H, I,
-                                 layout.q4_tiles(g_raw, g_s, gs, off, gu_inter=I), layout.q4_tiles(d_raw, d_s, gs, off),
-                                 eexp))
+            # the expert's bytes as moelan holds them, laid out on the device by the library's packer
+            ex = SimpleNamespace(gu=SimpleNamespace(raw=g_raw, s=g_s, gs=gs, offset=off),
+                                 down=SimpleNamespace(raw=d_raw, s=d_s, gs=gs, offset=off), inter=I)
+            packed = pack_expert_on(ex, dev)
+            if packed is None:
+                layout._check(H, gs)
+                layout._check(I, gs)
+                raise ValueError(f"moe_q4: experts with H={H}, I={I}, gs={gs} have no tile layout")
+            pool.put(key, packed)
         order[key] = None
         order.move_to_end(key)
         keys.append(key)
@@ -191,6 +196,10 @@ def _moe_q4(x, items, H, I, gs, out):
         pool.pop(order.popitem(last=False)[0])
     xd = torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(dev)
     uniq, part, status = pool.compute(xd, keys, [r for _, r, _ in items], [w for _, _, w in items])
-    out[uniq] += part.cpu().numpy()
-    if int(status.item()):
-        raise RuntimeError(f"moe_q4: the GPU kernels reported status {int(status.item())}")
+    res, st = pool.read_back(part, status)
+    if st:
+        raise RuntimeError(f"moe_q4: the GPU kernels reported status {st}")
+    if len(uniq) and uniq[0] == 0 and uniq[-1] == len(uniq) - 1:   # rows 0..U-1 (sorted, unique): a slice
+        out[:len(uniq)] += res
+    else:
+        out[uniq] += res

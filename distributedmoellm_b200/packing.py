@@ -101,3 +101,85 @@ def pack_expert(expert, inter: int | None = None):
     except ValueError:          # a group size the tile layout does not take
         return None
     return Packed(fg, fd, gu[3], H, I, gt, dt, (eg, ed, layout.act_exponent(l1, I)))
+
+
+def _dims(mat):
+    """(rows, columns) of a matrix as _as_group_matrix gives it."""
+    kind, payload, s = mat[0], mat[1], mat[2]
+    if kind == "q4":
+        return payload.shape[0], 2 * payload.shape[1]
+    if kind == "q8":
+        return payload.shape
+    return payload.shape[0], int(s)
+
+
+def _meta(mat, inter: int):
+    """(fmt, weight exponent, per-row |w| sums or None) of one matrix, from its
+    scales and bytes on the host; ``inter`` > 0 for a gate|up matrix."""
+    kind, payload, s, gs, off = mat
+    if kind == "q4":
+        return (layout.fmt_of("q4", s), layout.weight_exponent(s, 8),
+                layout.row_l1_q4(payload, s, gs, off) if inter else None)
+    if kind == "q8":
+        return (layout.fmt_of("q8", s), layout.weight_exponent(s, 128),
+                layout.row_l1_q8(payload, s, gs) if inter else None)
+    amax, l1 = layout.q4k_weight_bound(payload, s)
+    return layout.FMT_Q4K_F32, layout.exponent_for(amax), l1
+
+
+def _pack_on(mat, inter: int, out, dev) -> None:
+    """Lay one matrix out into the device bytes ``out`` with the library's
+    packers (mb_pack_q4 / mb_pack_q8 / mb_pack_q4k), from its bytes as stored."""
+    import torch
+
+    from . import device as D
+    kind, payload, s, gs, off = mat
+
+    def up(a, dt=None):
+        return torch.from_numpy(np.ascontiguousarray(a if dt is None else a.astype(dt, copy=False))).to(dev)
+
+    if kind == "q4":
+        D.pack_q4(up(payload, np.uint8), up(s, np.float16 if s.dtype == np.float16 else np.float32), gs, off,
+                  inter, out=out)
+    elif kind == "q8":
+        D.pack_q8(up(payload, np.int8), up(s, np.float16 if s.dtype == np.float16 else np.float32), gs, inter,
+                  out=out)
+    else:
+        D.pack_q4k(up(payload, np.uint8), int(s), inter, out=out)
+
+
+def pack_expert_on(expert, device, inter: int | None = None, max_bytes: int | None = None):
+    """As :func:`pack_expert`, but the tiles are laid out on ``device`` by the
+    library's packers from the matrices' bytes as moelan holds them, so only
+    those bytes cross to the device and no host re-layout runs.  The Packed's
+    ``gu_tiles`` / ``dn_tiles`` are views of one device buffer ``Packed.buf``
+    (gate|up tiles, then the down tiles at a 256-byte boundary).  None where
+    :func:`pack_expert` gives None, or when the buffer would exceed
+    ``max_bytes`` (then nothing is allocated)."""
+    import torch
+    gu, dn = _as_group_matrix(expert.gu), _as_group_matrix(expert.down)
+    if gu is None or dn is None or gu[3] != dn[3]:
+        return None
+    I = int(inter if inter is not None else expert.inter)
+    try:
+        (Og, Kg), (Od, Kd) = _dims(gu), _dims(dn)
+        for K, gs in ((Kg, gu[3]), (Kd, dn[3])):
+            layout._check(K, gs)
+        fg, eg, l1 = _meta(gu, I)
+        fd, ed, _ = _meta(dn, 0)
+    except ValueError:          # a group size the tile layout does not take
+        return None
+    H = Od
+    ng = layout.tiles_nbytes(fg, Og, Kg, gu_inter=I)
+    nd = layout.tiles_nbytes(fd, Od, Kd)
+    off = (ng + 255) // 256 * 256
+    if max_bytes is not None and off + nd > max_bytes:
+        return None
+    dev = torch.device(device)
+    buf = torch.empty(off + nd, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _pack_on(gu, I, buf[:ng], dev)
+        _pack_on(dn, 0, buf[off:off + nd], dev)
+    p = Packed(fg, fd, gu[3], H, I, buf[:ng], buf[off:off + nd], (eg, ed, layout.act_exponent(l1, I)))
+    p.buf, p.dn_offset = buf, off
+    return p

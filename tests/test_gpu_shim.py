@@ -159,3 +159,42 @@ def test_gpu_tier_launch_collect_and_stats():
     assert 0.0 < share < 1.0 and tier.used == 0
     b = bench_gpu("cuda", 1 << 30, H, I, "int4", 32, make_expert=lambda h, i, f, g: int4_expert(rng, h, i, g)[0])
     assert b["gpu_experts"] > 0 and b["gpu_ms"] > 0
+
+
+def _gguf_expert(rng, H, I, qt_gu, qt_dn):
+    from distributedmoellm_b200 import synthetic as S
+    g = NS(raw=S.gguf_rows(rng, I, H, qt_gu), qtype=qt_gu, shape=(I, H))
+    u = NS(raw=S.gguf_rows(rng, I, H, qt_gu), qtype=qt_gu, shape=(I, H))
+    d = NS(raw=S.gguf_rows(rng, H, I, qt_dn), qtype=qt_dn, shape=(H, I))
+    return NS(gu=NS(parts=(g, u)), down=d, inter=I)
+
+
+def test_experts_laid_out_on_the_device_match_the_host_layout(K):
+    """packing.pack_expert_on (the GPU tier's and moe_q4's upload: moelan's
+    bytes to the device, laid out there by mb_pack_*) gives the bytes and
+    exponents of the host layout (packing.pack_expert) for every packed form."""
+    import torch
+
+    from distributedmoellm_b200 import synthetic as S
+    from distributedmoellm_b200.packing import pack_expert, pack_expert_on
+    rng = np.random.default_rng(23)
+    H, I = 256, 384
+    cases = [int4_expert(rng, H, I, 32)[0], int4_expert(rng, H, I, 64, f16=True)[0]]
+    gr, gsc, dr, dsc = S.int4_expert(rng, H, I, 32, f16_scales=False)
+    cases.append(NS(gu=packed4(gr ^ 0x88, gsc, 32, offset=True), down=packed4(dr ^ 0x88, dsc, 32, offset=True),
+                    inter=I))
+    gq, gs8, dq, ds8 = S.int8_expert(rng, H, I, 64)
+    cases.append(NS(gu=NS(q=gq, s=gs8, gs=64), down=NS(q=dq, s=ds8, gs=64), inter=I))
+    cases += [_gguf_expert(rng, 512, 512, 12, 8), _gguf_expert(rng, 512, 512, 2, 2), _gguf_expert(rng, 256, 256, 8, 8)]
+    for i, ex in enumerate(cases):
+        want = pack_expert(ex)
+        got = pack_expert_on(ex, "cuda")
+        assert want is not None and got is not None, i
+        assert got.signature == want.signature and tuple(got.eexp) == tuple(want.eexp), i
+        torch.cuda.synchronize()
+        assert np.array_equal(got.gu_tiles.cpu().numpy(), want.gu_tiles), i
+        assert np.array_equal(got.dn_tiles.cpu().numpy(), want.dn_tiles), i
+        assert got.buf.numel() == got.dn_offset + want.dn_tiles.nbytes and got.dn_offset % 256 == 0
+        assert pack_expert_on(ex, "cuda", max_bytes=got.buf.numel() - 1) is None
+    dense = NS(gu=NS(w=np.zeros((2 * I, H), np.float32)), down=NS(w=np.zeros((H, I), np.float32)), inter=I)
+    assert pack_expert_on(dense, "cuda") is None

@@ -20,6 +20,7 @@ sys.path.insert(0, str(ROOT))
 
 from distributedmoellm_b200 import accel as A  # noqa: E402
 from distributedmoellm_b200 import kernels as K  # noqa: E402
+from distributedmoellm_b200 import packing as P  # noqa: E402
 from distributedmoellm_b200 import synthetic as S  # noqa: E402
 
 
@@ -41,9 +42,12 @@ def cpu_kernels(monkeypatch):
         uniq = np.unique(allr)
         return uniq, torch.ones((len(uniq), x.shape[1])), torch.zeros(1, dtype=torch.int32)
 
+    # the device packer's stand-in: the same tiles, laid out on the host
+    monkeypatch.setattr(K, "pack_expert_on", lambda ex, dev, inter=None, max_bytes=None: P.pack_expert(ex, inter))
     monkeypatch.setattr(K.D, "matmul_t", fake_matmul)
     monkeypatch.setattr(K.D, "gguf_matmul_t", fake_gguf)
     monkeypatch.setattr(A.DevicePool, "compute", fake_compute)
+    monkeypatch.setattr(A.DevicePool, "read_back", lambda self, part, status: (part.numpy(), int(status.item())))
     K._mats.clear()
     K._pool.clear()
     yield
