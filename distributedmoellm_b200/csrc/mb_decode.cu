@@ -306,16 +306,20 @@ struct WinCursor {
 // One row tile of one MMA warp: its block (16 rows x 128 columns) of a tile in
 // shared memory against the activation fragments bf, group scales applied in
 // f32 (and for the affine format the group biases times the rows' group sums
-// xs), the partial sums stored to rt ([input row][16 rows]).  TWO: the second N
-// tile (input rows 4..7) is live.  (A warp whose quad lies beyond K in this K
-// window stores zeros instead: see the MMA warps' loop.)
+// xs), the partial sums stored to rt ([input row][16 rows]).  has: the warp's
+// quad exists in this K window (else its partials are zero).  TWO: the second N
+// tile (input rows 4..7) is live.  The plain int4 formats test `has` once per
+// item in the caller (always true here: fewer instructions per tile, measured
+// faster); the int8 and affine formats test it per tile, which keeps their
+// register allocation (the hoisted form spilled more there and measured
+// slower on the Mixtral GGUF layer).
 template <bool Q8, bool F16S, bool AFF, bool TWO>
-__device__ __forceinline__ void tile_mma(const uint8_t* __restrict__ blk, const uint32_t (&bf)[2][4][4],
+__device__ __forceinline__ void tile_mma(const uint8_t* __restrict__ blk, bool has, const uint32_t (&bf)[2][4][4],
                                          const float (&xs)[2][4], float* __restrict__ rt, int t, int g)
 {
     constexpr int kData = Q8 ? 2048 : 1024;
     float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [N tile][row g, row g+8] of input row 4nt + t
-    {
+    if ((!Q8 && !AFF) || has) {
         const uint8_t* wp = blk + g * 64 + t * 16;
         const uint8_t* sp = blk + kData + g * (F16S ? 8 : 16);
         uint32_t wg[Q8 ? 8 : 4], wh[Q8 ? 8 : 4];
@@ -740,16 +744,16 @@ __global__ void __launch_bounds__(kThreadsMax, 1) moe_decode_kernel(const __grid
         if (it >= NR) MB_DECODE_WAIT(&rempty[r], rph ^ 1u, a.status, abort_flag);
         const bool ok = MB_DECODE_WAIT(&full[s], ph, a.status, abort_flag);
         float* rb = red + r * red_buf + warp * MT * kRedTile;
-        if (ok && has) {
+        if (ok && (Q8 || AFF || has)) {
             const uint8_t* stage = stages + (size_t)s * stage_bytes + warp * kBlock;
             if (two) {
                 for (int mt = 0; mt < ntiles; ++mt)
-                    tile_mma<Q8, F16S, AFF, true>(stage + mt * wt_bytes, bf, xs, rb + mt * kRedTile, t, g);
+                    tile_mma<Q8, F16S, AFF, true>(stage + mt * wt_bytes, has, bf, xs, rb + mt * kRedTile, t, g);
             } else {
                 for (int mt = 0; mt < ntiles; ++mt)
-                    tile_mma<Q8, F16S, AFF, false>(stage + mt * wt_bytes, bf, xs, rb + mt * kRedTile, t, g);
+                    tile_mma<Q8, F16S, AFF, false>(stage + mt * wt_bytes, has, bf, xs, rb + mt * kRedTile, t, g);
             }
-        } else {   // a failed wait, or no quad of this warp in this K window: zero partials
+        } else {   // a failed wait, or (plain int4) no quad of this warp in this K window: zero partials
             for (int mt = 0; mt < ntiles; ++mt) {
                 float* rt = rb + mt * kRedTile;
                 rt[t * 16 + g] = rt[t * 16 + g + 8] = rt[(4 + t) * 16 + g] = rt[(4 + t) * 16 + g + 8] = 0.f;
