@@ -159,3 +159,33 @@ def test_package_install_stays_callable(monkeypatch):
         saved = mb.install(pkg)
         assert callable(mb.install) and callable(mb.uninstall)
         mb.uninstall(saved)
+
+
+def test_device_packing_bookkeeping_matches_the_host_layout():
+    """packing.pack_expert_on lays experts out on the device; its formats,
+    exponents and tile sizes (worked out on the host before the packers run)
+    must be the host layout's, for every packed form."""
+    from distributedmoellm_b200 import packing as P
+    rng = np.random.default_rng(9)
+    H, I = 256, 384
+    gr, gsc, dr, dsc = S.int4_expert(rng, H, I, 32, f16_scales=False)
+    cases = [NS(gu=packed4(gr, gsc, 32), down=packed4(dr, dsc, 32), inter=I),
+             NS(gu=packed4(gr ^ 0x88, gsc.astype(np.float16), 32, offset=True),
+                down=packed4(dr ^ 0x88, dsc.astype(np.float16), 32, offset=True), inter=I)]
+    gq, gs_, dq, ds = S.int8_expert(rng, H, I, 64)
+    cases.append(NS(gu=NS(q=gq, s=gs_, gs=64), down=NS(q=dq, s=ds, gs=64), inter=I))
+    for qg, qd, Hm, Im in ((12, 8, 512, 512), (2, 2, 512, 512), (8, 8, 256, 256)):
+        g = NS(raw=S.gguf_rows(rng, Im, Hm, qg), qtype=qg, shape=(Im, Hm))
+        u = NS(raw=S.gguf_rows(rng, Im, Hm, qg), qtype=qg, shape=(Im, Hm))
+        d = NS(raw=S.gguf_rows(rng, Hm, Im, qd), qtype=qd, shape=(Hm, Im))
+        cases.append(NS(gu=NS(parts=(g, u)), down=d, inter=Im))
+    for i, ex in enumerate(cases):
+        want = P.pack_expert(ex)
+        gu, dn = P._as_group_matrix(ex.gu), P._as_group_matrix(ex.down)
+        (Og, Kg), (Od, Kd) = P._dims(gu), P._dims(dn)
+        fg, eg, l1 = P._meta(gu, ex.inter)
+        fd, ed, _ = P._meta(dn, 0)
+        assert (fg, fd, Od, ex.inter) == (want.fmt_gu, want.fmt_down, want.H, want.I), i
+        assert (eg, ed, L.act_exponent(l1, ex.inter)) == tuple(want.eexp), i
+        assert L.tiles_nbytes(fg, Og, Kg, gu_inter=ex.inter) == want.gu_tiles.nbytes, i
+        assert L.tiles_nbytes(fd, Od, Kd) == want.dn_tiles.nbytes, i
