@@ -49,14 +49,16 @@ def _key(*arrays):
 
 
 def _tiles(key, make, keep):
-    """The cached device copy for ``key`` (made by ``make()`` on a miss); call with _lock held."""
-    key = key + (_dev().index,)
+    """The cached device bytes for ``key`` (made by ``make(dev)`` on a miss: (fmt,
+    O, K, device tensor)); call with _lock held."""
+    dev = _dev()
+    key = key + (dev.index,)
     hit = _mats.get(key)
     if hit is not None:
         _mats.move_to_end(key)
         return hit
-    fmt, O, K, tiles = make()
-    ent = (torch.from_numpy(tiles).to(_dev()), fmt, O, K, keep)
+    fmt, O, K, tiles = make(dev)
+    ent = (tiles, fmt, O, K, keep)
     _mats[key] = ent
     while len(_mats) > _CACHE_MAX:
         _mats.popitem(last=False)
@@ -95,18 +97,33 @@ def gguf_dequant(raw: np.ndarray, qtype: int, out: np.ndarray) -> np.ndarray:
 
 
 # ---- single matrices: x @ W.T (moelan/kernels.py:981-998, 1018-1032) ----------------
+# A matrix's bytes go to the device as moelan holds them; the library's packers
+# lay them out there (mb_pack_q4 / mb_pack_q8).
+
+def _up(a, dtype, dev):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype)).to(dev)
+
+
+def _scales(s):
+    """Scales as the packers take them: f16 stays f16, anything else f32."""
+    return np.float16 if np.asarray(s).dtype == np.float16 else np.float32
+
 
 def q4_matmul_t(x: np.ndarray, raw: np.ndarray, s: np.ndarray, gs: int, offset: bool) -> np.ndarray:
     """x @ W.T for colibri int4 bytes; ``offset`` means raw was XOR-ed with 0x88."""
-    def make():
+    def make(dev):
         O, K = raw.shape[0], raw.shape[1] * 2
-        return layout.fmt_of("q4", s), O, K, layout.q4_tiles(raw, s, gs, offset)
+        layout._check(K, gs)
+        return (layout.fmt_of("q4", s), O, K,
+                D.pack_q4(_up(raw, np.uint8, dev), _up(s, _scales(s), dev), gs, bool(offset)))
     return _matmul(_key(raw, s) + (gs, bool(offset)), make, (raw, s), x)
 
 
 def q8_matmul_t(x: np.ndarray, q: np.ndarray, s: np.ndarray, gs: int) -> np.ndarray:
-    def make():
-        return layout.fmt_of("q8", s), q.shape[0], q.shape[1], layout.q8_tiles(q, s, gs)
+    def make(dev):
+        layout._check(q.shape[1], gs)
+        return (layout.fmt_of("q8", s), q.shape[0], q.shape[1],
+                D.pack_q8(_up(q, np.int8, dev), _up(s, _scales(s), dev), gs))
     return _matmul(_key(q, s) + (gs,), make, (q, s), x)
 
 
@@ -118,17 +135,19 @@ def gguf_matmul_t(x: np.ndarray, raw: np.ndarray, qtype: int, cols: int) -> np.n
     qtype = int(qtype)
     if qtype in (8, 2):
         if qtype == 8:
-            def make():
+            def make(dev):
                 q, d = layout.q8_0_as_q8(raw, cols)
-                return layout.FMT_Q8_F16, raw.shape[0], cols, layout.q8_tiles(q, d, 32)
+                return (layout.FMT_Q8_F16, raw.shape[0], cols,
+                        D.pack_q8(_up(q, np.int8, dev), _up(d, np.float16, dev), 32))
         else:
-            def make():
+            def make(dev):
                 r, d = layout.q4_0_as_q4(raw, cols)
-                return layout.FMT_Q4_F16, raw.shape[0], cols, layout.q4_tiles(r, d, 32, True)
+                return (layout.FMT_Q4_F16, raw.shape[0], cols,
+                        D.pack_q4(_up(r, np.uint8, dev), _up(d, np.float16, dev), 32, True))
         return _matmul(_key(raw) + (qtype, cols), make, (raw,), x)
 
-    def make_raw():
-        return 0, raw.shape[0], cols, np.ascontiguousarray(raw, np.uint8)
+    def make_raw(dev):
+        return 0, raw.shape[0], cols, _up(raw, np.uint8, dev)
     with _lock:
         t, _, _, _, _ = _tiles(_key(raw) + (qtype, cols, "raw"), make_raw, (raw,))
         xd = torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(t.device)

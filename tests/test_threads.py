@@ -44,6 +44,11 @@ def cpu_kernels(monkeypatch):
 
     # the device packer's stand-in: the same tiles, laid out on the host
     monkeypatch.setattr(K, "pack_expert_on", lambda ex, dev, inter=None, max_bytes=None: P.pack_expert(ex, inter))
+    # and for single matrices: the host layout's bytes as a (CPU) tensor
+    monkeypatch.setattr(K.D, "pack_q4", lambda raw, sc, gs, offset, inter=0, out=None: torch.from_numpy(
+        K.layout.q4_tiles(raw.numpy(), sc.numpy(), gs, offset, gu_inter=inter)))
+    monkeypatch.setattr(K.D, "pack_q8", lambda q, sc, gs, inter=0, out=None: torch.from_numpy(
+        K.layout.q8_tiles(q.numpy(), sc.numpy(), gs, gu_inter=inter)))
     monkeypatch.setattr(K.D, "matmul_t", fake_matmul)
     monkeypatch.setattr(K.D, "gguf_matmul_t", fake_gguf)
     monkeypatch.setattr(A.DevicePool, "compute", fake_compute)
