@@ -7,7 +7,8 @@
 //
 // Two launches per layer (gate|up -> activations, down -> y) of one
 // persistent, warp-specialised kernel: one CTA per SM walks work items
-// (expert, block of 128 weight rows) with
+// (expert, pass of at most 160 of its picks, block of 128 weight rows), dealt
+// round-robin over the CTAs, with
 //  * a weight producer warp: the packed tiles (the same HBM tile layout the
 //    decode kernels read) in 1-D bulk copies into a shared-memory ring;
 //  * a token producer warp: the expert's tokens, gathered once per layer
@@ -17,7 +18,7 @@
 //    arithmetic (exact until the one rounding of the product), written with
 //    tcgen05.st straight into tensor memory, where tcgen05.mma reads its A
 //    operand (the converted weights never pass through shared memory);
-//  * one MMA thread: tcgen05.mma M=128, N <= 192 tokens, K=16, f32
+//  * one MMA thread: tcgen05.mma M=128, N <= 160 tokens, K=16, f32
 //    accumulators in TMEM, two accumulator buffers;
 //  * four epilogue warps: tcgen05.ld, undo the power-of-two scalings, form
 //    SiLU(gate) * up (written as f16 for the down GEMM) or the f32 output
